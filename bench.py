@@ -1,0 +1,372 @@
+"""Benchmark of the batched sampler: sampled rows/s and HBM GB/s against the measured peak.
+
+Workload (the metric point): B=256 rows per GPU, V=151,936, float32 logits with config 3's
+distribution (Gumbel background + Zipf-ranked head) and parameters (T 0.7, top-p 0.95,
+min-p 0.05, repetition 1.1, frequency 0.3, presence 0.2, 2,048-id histories), seeded per rank.
+A step is one ``lss_sample`` call (history dedup + the per-row cluster kernel) over the batch;
+with N GPUs each rank samples its own 256 rows (weak scaling) and the token ids are gathered
+to rank 0 with NCCL inside the step.
+
+``--impl reference`` times the reference's CPU implementation of the same path (the
+``oracle.torch_port`` restatement of ``sample_next_token``, per-row loop, all host threads)
+on a bounded sample of the same rows.
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "sampled rows/s & HBM GB/s vs peak at B=256 V=151936; 1/2/4/8 GPU"
+B_PER_GPU = 256
+V = 151_936
+NBUF = 4  # rotating input buffers: 4 x 155.6 MB > L2 (126 MB), so every step reads cold
+
+
+def algorithmic_bytes(w) -> int:
+    """Bytes one call must move: logits once, history ids and offsets, params, uniform, token."""
+    esize = 4 if w.dtype == "f32" else 2
+    return int(w.B * w.V * esize + w.hist_ids.size * 4 + (w.B + 1) * 4 + w.B * (7 * 4 + 4 + 4))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_reference_rate(w, seconds: float = 12.0, min_rows: int = 8):
+    """Rows/s of the reference's per-row CPU sampler on this host (bounded sample)."""
+    from oracle import torch_port as TP
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(0)
+    TP.sample_workload_rows(w, [0], gen)  # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while n < min_rows or (time.perf_counter() - t0 < seconds and n < w.B):
+        TP.sample_workload_rows(w, [n % w.B], gen)
+        n += 1
+    dt = time.perf_counter() - t0
+    return n / dt, threads, n, dt
+
+
+def make_workload(rank: int):
+    from localstrm_b200 import workloads as wl
+    return wl.headline(seed=rank, B=B_PER_GPU, V=V)
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    w = make_workload(0)
+    rates = []
+    meta = None
+    for i in range(args.warmup + args.steps):
+        rate, cores, n, dt = cpu_reference_rate(w, seconds=args.cpu_seconds / max(args.steps, 1),
+                                                min_rows=4)
+        if i >= args.warmup:
+            rates.append(rate)
+            meta = (cores, n, dt)
+    value = statistics.median(rates)
+    cores, n, dt = meta
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * B_PER_GPU / value, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; config 3 distribution)",
+        "config": {"workload": "headline: B=256 V=151936 f32, config-3 params", "global_batch": B_PER_GPU,
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": cores, "kind": "port",
+                         "sample": f"{n} rows of the workload per step (~{dt:.1f} s), per-row "
+                                   "sample_next_token restated in torch CPU ops"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import torch.distributed as dist
+    from localstrm_b200 import _lib
+    from localstrm_b200.sampling import BatchSampler, RowParams
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+    w = make_workload(rank)
+    B = w.B
+    logits_host = torch.from_numpy(w.logits).pin_memory()
+    bufs = [logits_host.to(dev) for _ in range(NBUF)]
+    prm = RowParams.from_arrays(dev, temperature=w.temperature, top_k=w.top_k, top_p=w.top_p,
+                                min_p=w.min_p, repetition_penalty=w.repetition_penalty,
+                                frequency_penalty=w.frequency_penalty, presence_penalty=w.presence_penalty)
+    h_off = torch.from_numpy(w.hist_offsets.astype(np.int32)).to(dev)
+    h_ids = torch.from_numpy(w.hist_ids.astype(np.int32)).to(dev)
+    H = int(h_ids.numel())
+    uni = torch.from_numpy(w.uniforms).to(dev)
+    tokens = torch.empty(B, dtype=torch.int32, device=dev)
+    gathered = torch.empty(B * world, dtype=torch.int32, device=dev)
+    s = BatchSampler(dev)
+    ws = s.workspace(B, w.V, H)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    P = lambda t: t.data_ptr()
+
+    def prepare():
+        _lib.check("lss_history_prepare", lib.lss_history_prepare(
+            B, w.V, P(h_off), P(h_ids), H, P(prm.temperature), P(prm.repetition_penalty),
+            P(prm.frequency_penalty), P(prm.presence_penalty), P(ws), ws.numel(), sp))
+
+    def rows(x):
+        _lib.check("lss_sample_rows", lib.lss_sample_rows(
+            P(x), 0, B, w.V, x.stride(0), P(prm.temperature), P(prm.top_k), P(prm.top_p),
+            P(prm.min_p), P(prm.repetition_penalty), P(prm.frequency_penalty),
+            P(prm.presence_penalty), P(h_off), H, P(uni), P(tokens), None, None, P(ws), ws.numel(), sp))
+
+    def gather():
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, tokens)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # warm-up
+    for i in range(args.warmup):
+        prepare()
+        rows(bufs[i % NBUF])
+        gather()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local_rank)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    reps = max(1, args.inner)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        for r in range(reps):
+            x = bufs[(i * reps + r) % NBUF]
+            if r == 0:
+                ev[i][0].record(stream)
+            prepare()
+            if r == 0:
+                ev[i][1].record(stream)
+            rows(x)
+            if r == 0:
+                ev[i][2].record(stream)
+            gather()
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    clk = clocks.stop()
+    kern_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    step_ms_each = [e[0].elapsed_time(e[2]) for e in ev]
+    n_steps_total = args.steps * reps
+    if world > 1:
+        t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / n_steps_total
+    value = B * world * n_steps_total / (elapsed_ms / 1000.0)
+
+    # roofline of the dominant kernel (lss_rows_kernel)
+    alg = algorithmic_bytes(w)
+    kern_avg_ms = statistics.mean(kern_ms)
+    achieved = alg / (kern_avg_ms / 1000.0) / 1e9
+    peak, peak_kind = peaks()
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get("lss_rows_kernel_headline_bytes_per_launch")
+        except (OSError, ValueError):
+            traffic = None
+
+    # end to end through the public API with host buffers (pinned), copies inside the timing
+    e2e = None
+    if args.e2e_steps > 0:
+        from localstrm_b200.sampling import sample_batch  # noqa: F401  (public API module)
+        host_u = torch.from_numpy(w.uniforms).pin_memory()
+        host_off = torch.from_numpy(w.hist_offsets.astype(np.int32)).pin_memory()
+        host_ids = torch.from_numpy(w.hist_ids.astype(np.int32)).pin_memory()
+        host_prm = {k: torch.from_numpy(np.asarray(getattr(w, k))).pin_memory()
+                    for k in ("temperature", "top_k", "top_p", "min_p", "repetition_penalty",
+                              "frequency_penalty", "presence_penalty")}
+        dev_x = torch.empty_like(bufs[0])
+        tok_host = torch.empty(B * world, dtype=torch.int32).pin_memory()
+        h2d = logits_host.numel() * 4 + host_u.numel() * 4 + host_off.numel() * 4 + \
+            host_ids.numel() * 4 + sum(t.numel() * 4 for t in host_prm.values())
+        d2h = tok_host.numel() * 4 if rank == 0 else B * 4
+
+        def e2e_step():
+            dev_x.copy_(logits_host, non_blocking=True)
+            for k, t in host_prm.items():
+                getattr(prm, k).copy_(t, non_blocking=True)
+            h_off.copy_(host_off, non_blocking=True)
+            h_ids.copy_(host_ids, non_blocking=True)
+            uni.copy_(host_u, non_blocking=True)
+            s.sample(dev_x, prm, h_off, h_ids, uni, tokens_out=tokens)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, tokens)
+                tok_host.copy_(gathered, non_blocking=True)
+            else:
+                tok_host[:B].copy_(tokens, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        a1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = a0.elapsed_time(a1)
+        if world > 1:
+            t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = {"value": B * world * args.e2e_steps / (e2e_ms / 1000.0), "unit": "rows/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "ms_per_step": e2e_ms / args.e2e_steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        rate, cores, n, dt = cpu_reference_rate(w, seconds=args.cpu_seconds)
+        cpu = {"value": rate, "unit": "rows/s", "cores": cores, "kind": "port",
+               "sample": f"{n} rows of the same workload (~{dt:.1f} s): per-row sample_next_token "
+                         f"restated in torch CPU ops (oracle/torch_port.py)"}
+
+    paths = s.row_paths(B)
+    flags = s.status()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; config 3 distribution at V=151,936)",
+            "config": {"workload": "headline: B=256 rows/GPU, V=151936 f32 logits, T0.7 p0.95 "
+                                   "mp0.05 rep1.1 freq0.3 pres0.2, H=2048",
+                       "global_batch": B * world, "rows_per_gpu": B, "vocab": w.V,
+                       "parallelism": f"rows{world}" if world > 1 else "single",
+                       "l2": f"{NBUF} rotating input buffers of {B * w.V * 4 / 1e6:.1f} MB (> 126 MB L2)",
+                       "inner_reps": reps},
+            "hbm_gbs": alg * world * n_steps_total / (elapsed_ms / 1000.0) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "lss_rows_kernel", "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": alg, "kernel_ms": kern_avg_ms},
+            "step_ms_median": statistics.median(step_ms_each),
+            "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
+            "gpu_launches": (2 if H > 0 else 1) * n_steps_total,
+            "row_paths": {str(k): int((paths == k).sum()) for k in np.unique(paths)},
+            "device_flags": flags,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--inner", type=int, default=1, help="calls per timed step")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world and world == 1 and args.gpus > 1:
+        print(json.dumps({"error": "run N>1 under torch.distributed.run"}), file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args, rank, world)  # CPU only; ranks other than 0 exit without work
+        return
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
