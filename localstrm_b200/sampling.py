@@ -129,12 +129,15 @@ class BatchSampler:
 
     def __init__(self, device: Union[int, str, torch.device, None] = None):
         self.lib = _lib.load()
-        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
-            else torch.device(device)
-        if self.device.type != "cuda":
+        dev = torch.device("cuda") if device is None else torch.device(device)
+        if dev.type != "cuda":
             raise RuntimeError("BatchSampler needs a CUDA device (there is no CPU path)")
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
         self._ws = None
         self._ws_bytes = 0
+        self._last_ws = None
 
     def workspace(self, B: int, V: int, hist_total: int) -> torch.Tensor:
         need = int(self.lib.lss_workspace_bytes(B, V, hist_total))
@@ -143,7 +146,8 @@ class BatchSampler:
             self._ws_bytes = need
         base = self._ws.data_ptr()
         off = (-base) % 256
-        return self._ws[off:off + need]
+        self._last_ws = self._ws[off:off + need]
+        return self._last_ws
 
     def sample(self, logits: torch.Tensor, params: RowParams, hist_offsets: Optional[torch.Tensor],
                hist_ids: Optional[torch.Tensor], uniforms: torch.Tensor,
@@ -181,11 +185,12 @@ class BatchSampler:
             hist_total, uniforms.data_ptr(), tokens_out.data_ptr(), ptr(kept_out), ptr(probs_out),
             ws.data_ptr(), ws.numel(), stream)
         _lib.check("lss_sample", st)
-        self._last_ws = ws
         return tokens_out
 
     def row_paths(self, B: int) -> np.ndarray:
         """Path codes of the last call (synchronises the stream)."""
+        if self._last_ws is None:
+            raise RuntimeError("no call has been made on this sampler yet")
         out = np.zeros(B, dtype=np.int32)
         stream = torch.cuda.current_stream(self.device).cuda_stream
         _lib.check("lss_read_row_paths", self.lib.lss_read_row_paths(
@@ -194,6 +199,8 @@ class BatchSampler:
 
     def status(self) -> int:
         """Device error flags of the last call (synchronises the stream)."""
+        if self._last_ws is None:
+            raise RuntimeError("no call has been made on this sampler yet")
         f = ctypes.c_uint32(0)
         stream = torch.cuda.current_stream(self.device).cuda_stream
         self.lib.lss_read_status(self._last_ws.data_ptr(), ctypes.byref(f), stream)
