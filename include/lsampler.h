@@ -47,6 +47,7 @@ extern "C" {
 #define LSS_ERR_CUDA 3          /* a CUDA runtime call failed (launch or attribute) */
 #define LSS_ERR_UNSUPPORTED 4   /* V larger than the largest supported row, or no sm_100 device */
 #define LSS_ERR_DEVICE 5        /* lss_read_status: the device reported an error flag */
+#define LSS_ERR_SCRATCH_LIMIT 6 /* lss_sample_noalloc: the call needs more than its fixed scratch */
 
 #define LSS_DTYPE_F32 0
 #define LSS_DTYPE_BF16 1
@@ -117,6 +118,31 @@ int lss_sample_rows(const void* logits, int dtype, int B, int V, int64_t row_str
  * all-greedy seam of the engine (llm_engine.py:1139-1141; torch.argmax semantics). */
 int lss_argmax(const void* logits, int dtype, int B, int V, int64_t row_stride,
                int32_t* tokens_out, void* stream);
+
+/* lss_sample without a caller-provided workspace; it allocates nothing.
+ * No counterpart in the reference: LocalStrm allocates through PyTorch on every call.
+ * It exists for callers that must not allocate device memory while they sample: a serving
+ * engine that reserved nearly all of the GPU for its paged KV cache at start-up (as
+ * LocalStrm's block pool and VRAM preflight do) cannot count on cudaMalloc succeeding in
+ * the middle of a decode step, and a cudaMalloc/cudaFree there can also synchronise the
+ * device and stall the other streams.
+ * Its scratch is one file-scope device array of LSS_NOALLOC_SCRATCH_BYTES (16 MiB) that
+ * every GPU which loads this library holds until the process exits.  A call whose
+ * lss_workspace_bytes(B, V, hist_total) exceeds that returns LSS_ERR_SCRATCH_LIMIT and
+ * launches nothing (256 rows with 2,048-id histories fit).  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture.  All calls on a device share the one
+ * array: two calls that overlap on the GPU (different streams, no ordering between them)
+ * race on it and give wrong tokens; serialise them.  Everything that must start at zero
+ * is cleared by the call itself.  lss_read_status / lss_read_row_paths do not apply. */
+#define LSS_NOALLOC_SCRATCH_BYTES (16u << 20)
+int lss_sample_noalloc(const void* logits, int dtype, int B, int V, int64_t row_stride,
+                       const float* temperature, const int32_t* top_k, const float* top_p,
+                       const float* min_p, const float* repetition_penalty,
+                       const float* frequency_penalty, const float* presence_penalty,
+                       const int32_t* hist_offsets, const int32_t* hist_ids,
+                       int64_t hist_total, const float* uniforms, int32_t* tokens_out,
+                       uint8_t* kept_out, float* probs_out, void* stream);
 
 /* Synchronises `stream`, then returns the device error flags accumulated in the
  * workspace since lss_sample last cleared them (0 when none). */

@@ -37,6 +37,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "lsampler.h"
 
@@ -1289,6 +1290,7 @@ const char* lss_status_string(int s) {
     case LSS_ERR_CUDA: return "CUDA runtime error";
     case LSS_ERR_UNSUPPORTED: return "unsupported size or device";
     case LSS_ERR_DEVICE: return "device reported an error flag";
+    case LSS_ERR_SCRATCH_LIMIT: return "request exceeds the fixed scratch of lss_sample_noalloc";
     default: return "unknown status";
   }
 }
@@ -1418,6 +1420,57 @@ int lss_sample(const void* logits, int dtype, int B, int V, int64_t row_stride, 
   return lss_sample_rows(logits, dtype, B, V, row_stride, temperature, top_k, top_p, min_p,
                          repetition_penalty, frequency_penalty, presence_penalty, hist_offsets, hist_total,
                          uniforms, tokens_out, kept_out, probs_out, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: the workspace is a fixed file-scope device array.
+// ---------------------------------------------------------------------------
+namespace lss {
+static __device__ __align__(256) unsigned char g_noalloc_scratch[LSS_NOALLOC_SCRATCH_BYTES];
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64] = {nullptr};
+
+// Device address of the scratch on the current device, looked up once per device.
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return LSS_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return LSS_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+      cudaGetLastError();
+      return LSS_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return LSS_OK;
+}
+}  // namespace lss
+
+extern "C" {
+
+int lss_sample_noalloc(const void* logits, int dtype, int B, int V, int64_t row_stride,
+                       const float* temperature, const int32_t* top_k, const float* top_p,
+                       const float* min_p, const float* repetition_penalty,
+                       const float* frequency_penalty, const float* presence_penalty,
+                       const int32_t* hist_offsets, const int32_t* hist_ids, int64_t hist_total,
+                       const float* uniforms, int32_t* tokens_out, uint8_t* kept_out, float* probs_out,
+                       void* stream) {
+  if (B < 0 || V < 1 || hist_total < 0) return LSS_ERR_INVALID_ARG;
+  if (B == 0) return LSS_OK;
+  const size_t need = lss_workspace_bytes(B, V, hist_total);
+  if (need == 0) return LSS_ERR_INVALID_ARG;
+  if (need > (size_t)LSS_NOALLOC_SCRATCH_BYTES) return LSS_ERR_SCRATCH_LIMIT;
+  void* ws = nullptr;
+  int rc = lss::noalloc_scratch(&ws);
+  if (rc != LSS_OK) return rc;
+  return lss_sample(logits, dtype, B, V, row_stride, temperature, top_k, top_p, min_p, repetition_penalty,
+                    frequency_penalty, presence_penalty, hist_offsets, hist_ids, hist_total, uniforms,
+                    tokens_out, kept_out, probs_out, ws, (size_t)LSS_NOALLOC_SCRATCH_BYTES, stream);
 }
 
 int lss_argmax(const void* logits, int dtype, int B, int V, int64_t row_stride, int32_t* tokens_out,

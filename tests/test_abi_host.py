@@ -93,3 +93,17 @@ def test_cpu_tensors_fail_loudly():
         S.sample_next_token(torch.zeros(4), S.SamplingParams.greedy())
     with pytest.raises(RuntimeError):
         S.sample_batch(torch.zeros(2, 4), [S.SamplingParams()] * 2)
+
+
+def test_noalloc_rejects_requests_beyond_its_fixed_scratch():
+    lib = _lib.load()
+    limit = 16 << 20
+    B, V = 256, 151_936
+    H = 1
+    while lib.lss_workspace_bytes(B, V, H) <= limit:
+        H *= 2
+    args = [1, 0, B, V, V] + [1] * 7 + [1, 1, H, 1, 1, None, None, None]
+    assert lib.lss_sample_noalloc(*args) == 6            # LSS_ERR_SCRATCH_LIMIT, nothing launched
+    assert "scratch" in _lib.status_string(6)
+    assert lib.lss_workspace_bytes(256, V, 256 * 2048) <= limit   # the headline fits
+    assert lib.lss_sample_noalloc(*([1, 0, 0, V, V] + [1] * 7 + [1, 1, 0, 1, 1, None, None, None])) == 0
