@@ -173,15 +173,17 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     P = lambda t: t.data_ptr()
 
     def prepare():
-        _lib.check("lss_history_prepare", lib.lss_history_prepare(
-            B, w.V, P(h_off), P(h_ids), H, P(prm.temperature), P(prm.repetition_penalty),
-            P(prm.frequency_penalty), P(prm.presence_penalty), P(ws), ws.numel(), sp))
+        _lib.check("lss_sample_prepare", lib.lss_sample_prepare(
+            B, w.V, P(prm.temperature), P(prm.top_k), P(prm.min_p), P(prm.repetition_penalty),
+            P(prm.frequency_penalty), P(prm.presence_penalty), P(h_off), P(h_ids), H, P(ws),
+            ws.numel(), sp))
 
     def rows(x):
         _lib.check("lss_sample_rows", lib.lss_sample_rows(
             P(x), 0, B, w.V, x.stride(0), P(prm.temperature), P(prm.top_k), P(prm.top_p),
             P(prm.min_p), P(prm.repetition_penalty), P(prm.frequency_penalty),
-            P(prm.presence_penalty), P(h_off), H, P(uni), P(tokens), None, None, P(ws), ws.numel(), sp))
+            P(prm.presence_penalty), P(h_off), P(h_ids), H, P(uni), P(tokens), None, None, P(ws), ws.numel(),
+            sp))
 
     def gather():
         if world > 1:
@@ -327,7 +329,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                          "algorithmic_bytes_per_launch": alg, "kernel_ms": kern_avg_ms},
             "step_ms_median": statistics.median(step_ms_each),
             "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
-            "gpu_launches": (2 if H > 0 else 1) * n_steps_total,
+            "gpu_launches": 3 * n_steps_total,
             "row_paths": {str(k): int((paths == k).sum()) for k in np.unique(paths)},
             "device_flags": flags,
         }

@@ -63,6 +63,7 @@ extern "C" {
 #define LSS_PATH_SPECIAL 2    /* NaN, +inf or all -inf after scaling: NaN-guard argmax */
 #define LSS_PATH_GATHER 3     /* survivors gathered into one CTA and resolved there */
 #define LSS_PATH_DENSE 4      /* cluster-wide radix select over the whole row */
+#define LSS_PATH_SLOW_GATHER 5 /* survivors gathered and resolved by the second kernel */
 
 /* Library version, (major << 16) | (minor << 8) | patch. */
 int lss_version(void);
@@ -96,23 +97,24 @@ int lss_sample(const void* logits, int dtype, int B, int V, int64_t row_stride,
                float* probs_out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* The two stages of lss_sample, for callers that overlap or time them separately.
- * lss_history_prepare clears the workspace status and turns the CSR histories into
- * per-row (id, count) pairs (torch.unique, sampling.py:52); it must precede
- * lss_sample_rows on the same stream whenever hist_total > 0.  lss_sample_rows runs
- * the per-row kernel (penalties, temperature, filters, draw); its hist_total must be
- * the value given to lss_history_prepare.  Arguments mean what they mean in lss_sample. */
-int lss_history_prepare(int B, int V, const int32_t* hist_offsets, const int32_t* hist_ids,
-                        int64_t hist_total, const float* temperature,
-                        const float* repetition_penalty, const float* frequency_penalty,
-                        const float* presence_penalty, void* workspace, size_t workspace_bytes,
-                        void* stream);
+ * lss_sample_prepare validates the arguments and clears the workspace status (error flags
+ * and the deferred-row count); it must precede lss_sample_rows on the same stream.
+ * lss_sample_rows runs the kernels: a streaming pass over the logits (history penalties,
+ * sampling.py:52-66, per-slice maxima and candidates), a per-row resolve (temperature,
+ * filters, draw) and a second kernel for the rows that need the whole vocabulary.
+ * Arguments mean what they mean in lss_sample. */
+int lss_sample_prepare(int B, int V, const float* temperature, const int32_t* top_k,
+                       const float* min_p, const float* repetition_penalty,
+                       const float* frequency_penalty, const float* presence_penalty,
+                       const int32_t* hist_offsets, const int32_t* hist_ids, int64_t hist_total,
+                       void* workspace, size_t workspace_bytes, void* stream);
 int lss_sample_rows(const void* logits, int dtype, int B, int V, int64_t row_stride,
                     const float* temperature, const int32_t* top_k, const float* top_p,
                     const float* min_p, const float* repetition_penalty,
                     const float* frequency_penalty, const float* presence_penalty,
-                    const int32_t* hist_offsets, int64_t hist_total, const float* uniforms,
-                    int32_t* tokens_out, uint8_t* kept_out, float* probs_out, void* workspace,
-                    size_t workspace_bytes, void* stream);
+                    const int32_t* hist_offsets, const int32_t* hist_ids, int64_t hist_total,
+                    const float* uniforms, int32_t* tokens_out, uint8_t* kept_out,
+                    float* probs_out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Batched greedy argmax (NaN counts as largest, lowest index wins ties), the
  * all-greedy seam of the engine (llm_engine.py:1139-1141; torch.argmax semantics). */
@@ -126,7 +128,7 @@ int lss_argmax(const void* logits, int dtype, int B, int V, int64_t row_stride,
  * LocalStrm's block pool and VRAM preflight do) cannot count on cudaMalloc succeeding in
  * the middle of a decode step, and a cudaMalloc/cudaFree there can also synchronise the
  * device and stall the other streams.
- * Its scratch is one file-scope device array of LSS_NOALLOC_SCRATCH_BYTES (16 MiB) that
+ * Its scratch is one file-scope device array of LSS_NOALLOC_SCRATCH_BYTES (32 MiB) that
  * every GPU which loads this library holds until the process exits.  A call whose
  * lss_workspace_bytes(B, V, hist_total) exceeds that returns LSS_ERR_SCRATCH_LIMIT and
  * launches nothing (256 rows with 2,048-id histories fit).  The first call on a device
@@ -135,7 +137,7 @@ int lss_argmax(const void* logits, int dtype, int B, int V, int64_t row_stride,
  * array: two calls that overlap on the GPU (different streams, no ordering between them)
  * race on it and give wrong tokens; serialise them.  Everything that must start at zero
  * is cleared by the call itself.  lss_read_status / lss_read_row_paths do not apply. */
-#define LSS_NOALLOC_SCRATCH_BYTES (16u << 20)
+#define LSS_NOALLOC_SCRATCH_BYTES (32u << 20)
 int lss_sample_noalloc(const void* logits, int dtype, int B, int V, int64_t row_stride,
                        const float* temperature, const int32_t* top_k, const float* top_p,
                        const float* min_p, const float* repetition_penalty,

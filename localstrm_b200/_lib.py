@@ -13,7 +13,7 @@ from . import build as _build
 
 LSS_OK = 0
 DTYPES = {"f32": 0, "bf16": 1, "f16": 2}
-PATHS = {1: "greedy", 2: "special", 3: "gather", 4: "dense"}
+PATHS = {1: "greedy", 2: "special", 3: "gather", 4: "dense", 5: "slow_gather"}
 
 _lib = None
 
@@ -39,10 +39,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.lss_sample.restype = c_int
     lib.lss_sample.argtypes = [P, c_int, c_int, c_int, c_int64, P, P, P, P, P, P, P, P, P, c_int64,
                                P, P, P, P, P, c_size_t, P]
-    lib.lss_history_prepare.restype = c_int
-    lib.lss_history_prepare.argtypes = [c_int, c_int, P, P, c_int64, P, P, P, P, P, c_size_t, P]
+    lib.lss_sample_prepare.restype = c_int
+    lib.lss_sample_prepare.argtypes = [c_int, c_int, P, P, P, P, P, P, P, P, c_int64, P, c_size_t, P]
     lib.lss_sample_rows.restype = c_int
-    lib.lss_sample_rows.argtypes = [P, c_int, c_int, c_int, c_int64, P, P, P, P, P, P, P, P, c_int64,
+    lib.lss_sample_rows.argtypes = [P, c_int, c_int, c_int, c_int64, P, P, P, P, P, P, P, P, P, c_int64,
                                     P, P, P, P, P, c_size_t, P]
     lib.lss_sample_noalloc.restype = c_int
     lib.lss_sample_noalloc.argtypes = [P, c_int, c_int, c_int, c_int64, P, P, P, P, P, P, P, P, P,

@@ -97,7 +97,7 @@ def test_cpu_tensors_fail_loudly():
 
 def test_noalloc_rejects_requests_beyond_its_fixed_scratch():
     lib = _lib.load()
-    limit = 16 << 20
+    limit = 32 << 20
     B, V = 256, 151_936
     H = 1
     while lib.lss_workspace_bytes(B, V, H) <= limit:

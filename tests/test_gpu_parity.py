@@ -62,7 +62,7 @@ def test_config3_full():
     out = G.run(w)
     assert out["flags"] == 0
     stats = check_workload(w, out)
-    assert set(stats) <= {2, 3, 4}
+    assert set(stats) <= {2, 3, 4, 5}
 
 
 @needs_cuda
@@ -79,7 +79,7 @@ def test_config2_bf16():
     out = G.run(w)
     assert out["flags"] == 0
     stats = check_workload(w, out)
-    assert stats.get(3, 0) + stats.get(4, 0) == w.B
+    assert stats.get(3, 0) + stats.get(4, 0) + stats.get(5, 0) == w.B
 
 
 @needs_cuda
