@@ -113,6 +113,22 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
   return true;
 }
+// Bounded wait that lets the thread sleep until the phase completes (suspend-time hint), for
+// waits that are not on the critical path of the waiting warp.
+__device__ __forceinline__ bool mbar_wait_bounded_sleep(uint64_t* bar, uint32_t parity) {
+  long long t0 = clock64();
+  for (;;) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, "
+        "p;\n}\n"
+        : "=r"(ok)
+        : "r"(saddr(bar)), "r"(parity), "r"(1000000u)
+        : "memory");
+    if (ok) return true;
+    if (clock64() - t0 > WAIT_CYCLES) return false;
+  }
+}
 // Generic-proxy shared-memory writes made before this call are ordered before later
 // bulk-copy (async-proxy) writes into the same memory.
 __device__ __forceinline__ void fence_proxy_async() {
@@ -220,6 +236,7 @@ __device__ T block_excl_scan(T v, T* scr, T& total) {
   return pre + x - v;
 }
 struct MaxF { __device__ float operator()(float a, float b) const { return fmax_nan(a, b); } };
+struct MaxU32 { __device__ uint32_t operator()(uint32_t a, uint32_t b) const { return a > b ? a : b; } };
 struct MaxU64 { __device__ uint64_t operator()(uint64_t a, uint64_t b) const { return a > b ? a : b; } };
 struct SumU64 { __device__ uint64_t operator()(uint64_t a, uint64_t b) const { return a + b; } };
 struct SumU32 { __device__ uint32_t operator()(uint32_t a, uint32_t b) const { return a + b; } };

@@ -212,7 +212,7 @@ static cudaError_t prepare_scan_kernel(K kern, KernelCfg& kc, int smem, int& nct
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     int per_sm = 0, nsm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NT, (size_t)smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, SC_NT, (size_t)smem);
     if (e != cudaSuccess) return e;
     e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
@@ -250,7 +250,7 @@ static cudaError_t launch_rows(const ScanArgs& sa, const RowArgs& ra, const Gath
   cudaError_t e = prepare_scan_kernel(lss_scan_kernel<DT>, scan_cfg, pl.scan_smem, nctas);
   if (e != cudaSuccess) return e;
   const int nitems = B * pl.S;
-  lss_scan_kernel<DT><<<std::min(nctas, nitems), NT, pl.scan_smem, st>>>(sa);
+  lss_scan_kernel<DT><<<std::min(nctas, nitems), SC_NT, pl.scan_smem, st>>>(sa);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   lss_resolve_kernel<<<B, NT, 0, st>>>(ra, ga);

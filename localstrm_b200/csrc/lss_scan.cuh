@@ -9,9 +9,10 @@
 //    when a stage of the two-stage ring is free it describes the item in shared memory and
 //    starts two bulk async copies into the stage — the slice of logits and the row's history
 //    ids — so the next slice streams in while the current one is processed.
-//  * 15 compute warps, per item: the history ids that fall in the slice are counted in a
-//    shared hash (torch.unique of the history, sampling.py:52) and the penalties applied
-//    once per unique id (sampling.py:55-66); the slice max of the pre-temperature values z
+//  * 31 compute warps, per item: the history ids that fall in the slice are counted in
+//    16-bit shared counters, one per vocabulary entry of the slice (torch.unique of the
+//    history, sampling.py:52), and the penalties applied once per unique id
+//    (sampling.py:55-66); the slice max of the pre-temperature values z
 //    (held in registers, so each logit is read from shared memory once); the candidate
 //    threshold; the candidates written to the item's segment in global memory and a 16-byte
 //    summary (slice max or argmax code, candidate count, flags).
@@ -28,41 +29,43 @@
 
 namespace lss {
 
-constexpr int SC_CW = NWARP - 1;              // compute warps
+constexpr int SC_NT = 1024;                   // threads per CTA
+constexpr int SC_CW = SC_NT / 32 - 1;         // compute warps
 constexpr int SC_CT = SC_CW * 32;             // compute threads
 constexpr int SC_PROD = SC_CW;                // index of the producer warp
-constexpr int SC_R = 10;                      // float4 of the slice per compute thread
-constexpr int SC_TS_MAX = SC_CT * SC_R * 4;   // logits per slice (19,200)
+constexpr int SC_R = 5;                       // float4 of the slice per compute thread
+constexpr int SC_TS_MAX = 19200;              // logits per slice (<= SC_CT * SC_R * 4)
+static_assert(SC_TS_MAX <= SC_CT * SC_R * 4, "a slice must fit the compute threads' registers");
 constexpr int SC_HB = 2048;                   // history ids staged per item
-constexpr int SC_HSLOTS = 2048;               // hash slots (unique ids of one slice)
-constexpr int SC_HSHIFT = 21;                 // 32 - log2(SC_HSLOTS)
+constexpr int SC_HMAX = 65535;                // longest history counted in 16-bit counters
 constexpr int SC_RING = 8;                    // parameter ring (items)
 constexpr int SC_AHEAD = 4;                   // parameters fetched this many items ahead
 constexpr int SC_BAR = 3;                     // named barrier of the compute warps
 constexpr int SC_SEG_MIN = 256;               // candidate slots per item (at least)
-constexpr uint32_t HASH_EMPTY = 0xffffffffu;
 
 constexpr int ITEM_END = 0, ITEM_SKIP = 1, ITEM_GREEDY = 2, ITEM_SAMPLE = 3;
 // Summary flags: NaN / +inf in the slice or y overflow; top-k window deeper than the bins;
-// more unique history ids in the slice than the hash holds.
+// a history longer than the 16-bit counters.
 constexpr uint32_t SUM_SPECIAL = 1u, SUM_FAR = 2u, SUM_HASH = 4u;
 
 struct __align__(16) ItemDesc {
   int row, slice, mode, nb;     // nb: bytes of the slice the bulk copy stages
   int hcount, hb, hlead, hbn;   // history: ids (0: no penalties), CSR base, staged window
-  float T, mp, rep, freq;
-  float pres;
-  int k, pad0, pad1;
+  float T, rep, freq, pres;
+  int k, lo, n, pad0;           // k: top-k when active (0 < k < V), else 0; slice [lo, lo + n)
+  float tl;                     // min-p: T * ln(min_p) (0: inactive), the floor's offset in z
+  float sb, binw, pad1;         // top-k bins: 16 / T per unit of z, and T / 16
 };
 struct __align__(16) ItemScratch {
-  unsigned long long best;      // greedy: argmax code of the slice
-  uint32_t maxk, flags, cnt, done, nslots, pad;
+  uint32_t cnt, flags, pad0, pad1;  // candidates, summary flags
 };
 struct __align__(16) ScanCtl {
   uint64_t full[2];             // stage landed (1 arrival + bytes)
   uint64_t empty[2];            // stage released (one arrival per compute warp)
   ItemDesc desc[2];
   ItemScratch sc[2];
+  uint64_t best[2][32];         // greedy items: argmax code per warp
+  uint32_t wkey[2][32];         // sampled items: max key of z per warp (all ones: NaN / +inf)
   uint32_t prm[SC_RING][8];     // T, k, min_p, rep, freq, pres, hist_off[row], hist_off[row+1]
 };
 
@@ -88,32 +91,39 @@ struct ScanArgs {
 
 __host__ __device__ constexpr int scan_stage_bytes(int tile_bytes) { return tile_bytes + SC_HB * 4; }
 __host__ __device__ constexpr int scan_smem_bytes(int tile_bytes) {
-  return 2 * scan_stage_bytes(tile_bytes) + SC_HSLOTS * 8 + SC_HSLOTS * 2 + (((NBIN + 1) * 4 + 15) & ~15) +
+  return 2 * scan_stage_bytes(tile_bytes) + SC_TS_MAX * 2 + (((NBIN + 1) * 4 + 15) & ~15) +
          (int)((sizeof(ScanCtl) + 15) & ~15);
+}
+
+// Penalties of one float4 of the slice from its four 16-bit history counts (zero: untouched).
+__device__ __noinline__ void apply4(float4* p, uint2 c, float rp, float fq, float pr) {
+  float4 x = *p;
+  if (c.x & 0xffffu) x.x = penalise(x.x, rp, fq, pr, (int)(c.x & 0xffffu));
+  if (c.x >> 16) x.y = penalise(x.y, rp, fq, pr, (int)(c.x >> 16));
+  if (c.y & 0xffffu) x.z = penalise(x.z, rp, fq, pr, (int)(c.y & 0xffffu));
+  if (c.y >> 16) x.w = penalise(x.w, rp, fq, pr, (int)(c.y >> 16));
+  *p = x;
 }
 
 __device__ __forceinline__ void sc_sync() { asm volatile("bar.sync %0, %1;" ::"n"(SC_BAR), "n"(SC_CT) : "memory"); }
 
 template <int DT>
-__global__ void __launch_bounds__(NT, 1) lss_scan_kernel(const ScanArgs a) {
+__global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
   constexpr int ES = DT == LSS_DTYPE_F32 ? 4 : 2;
   extern __shared__ __align__(1024) unsigned char smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int stage_bytes = scan_stage_bytes(a.tile_bytes);
-  uint32_t* hkeys = reinterpret_cast<uint32_t*>(smem + 2 * stage_bytes);
-  uint32_t* hcnts = hkeys + SC_HSLOTS;
-  uint16_t* hlist = reinterpret_cast<uint16_t*>(hcnts + SC_HSLOTS);
-  uint32_t* HL = reinterpret_cast<uint32_t*>(hlist + SC_HSLOTS);
+  // History counts of the slice: two 16-bit counters per word (entry i in word i / 2), zero
+  // between items (each compute thread resets the counters of its own entries).
+  uint32_t* hcnt2 = reinterpret_cast<uint32_t*>(smem + 2 * stage_bytes);
+  uint32_t* HL = hcnt2 + SC_TS_MAX / 2;
   ScanCtl* ctl = reinterpret_cast<ScanCtl*>(reinterpret_cast<unsigned char*>(HL) + (((NBIN + 1) * 4 + 15) & ~15));
   const int V = a.V, S = a.S, TS = a.TS;
   const int nitems = a.B * S;
   const int G = gridDim.x;
 
-  for (int i = tid; i < SC_HSLOTS; i += NT) {
-    hkeys[i] = HASH_EMPTY;
-    hcnts[i] = 0;
-  }
-  if (tid < (int)(2 * sizeof(ItemScratch) / 4)) reinterpret_cast<uint32_t*>(ctl->sc)[tid] = 0u;
+  for (int i = tid; i < SC_TS_MAX / 2; i += SC_NT) hcnt2[i] = 0u;
+  if (tid < (int)(2 * sizeof(ItemScratch) / 4)) reinterpret_cast<uint32_t*>(ctl->sc)[tid] = 0u;  // cnt, flags
   if (tid == 0) {
     mbar_init(&ctl->full[0], 1);
     mbar_init(&ctl->full[1], 1);
@@ -156,15 +166,19 @@ __global__ void __launch_bounds__(NT, 1) lss_scan_kernel(const ScanArgs a) {
       __syncwarp();
       fetch(j + SC_AHEAD);
       if (lane == 0) {
-        if (j >= 2 && !mbar_wait_bounded(&ctl->empty[s], (uint32_t)(((j >> 1) - 1) & 1)))
-          atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
-        ItemDesc& d = ctl->desc[s];
-        if (t >= nitems) {
-          d.mode = ITEM_END;
-          mbar_expect_tx(&ctl->full[s], 0u);
-        } else {
+        // The item is described before its stage is free, so that only the stores and the
+        // copies follow the wait.
+        ItemDesc nd{};
+        const char* g0 = nullptr;
+        uintptr_t w0 = 0;
+        nd.mode = ITEM_END;
+        if (t < nitems) {
           const uint32_t* p = ctl->prm[j % SC_RING];
-          const int row = t / S, slice = t - row * S;
+          // Slices rotate with the row, so that every CTA meets every slice of the vocabulary
+          // (the grid size and S share factors; without it a CTA would see two slices only).
+          const int row = t / S;
+          int slice = t - row * S + row;
+          slice -= (slice / S) * S;
           const float T = __uint_as_float(p[0]);
           const int k = (int)p[1];
           const float mp = __uint_as_float(p[2]);
@@ -177,14 +191,13 @@ __global__ void __launch_bounds__(NT, 1) lss_scan_kernel(const ScanArgs a) {
           const int mode = !bounded ? ITEM_SKIP : greedy ? ITEM_GREEDY : ITEM_SAMPLE;
           const int lo = slice * TS;
           const int n = min(V, lo + TS) - lo;
-          const char* g0 = reinterpret_cast<const char*>(a.logits) + ((int64_t)row * a.row_stride + lo) * ES;
+          g0 = reinterpret_cast<const char*>(a.logits) + ((int64_t)row * a.row_stride + lo) * ES;
           const int nb = (mode != ITEM_SKIP && (reinterpret_cast<uintptr_t>(g0) & 15) == 0) ? ((n * ES) & ~15) : 0;
           const int H = h1 - h0;
           const bool pen = mode == ITEM_SAMPLE && a.use_hist && H > 0 && (rp != 1.0f || fq != 0.0f || pr != 0.0f);
           // History window: the 16-byte blocks that cover ids [h0, h1), clipped to the
           // 16-byte blocks inside the id array, at most SC_HB ids.
           int hlead = 0, hbn = 0;
-          uintptr_t w0 = 0;
           if (pen) {
             const uintptr_t lo_ok = (hbase + 15) & ~(uintptr_t)15;
             const uintptr_t hi_ok = (hbase + 4 * (uintptr_t)a.hist_total) & ~(uintptr_t)15;
@@ -198,28 +211,35 @@ __global__ void __launch_bounds__(NT, 1) lss_scan_kernel(const ScanArgs a) {
               hlead = (int)((intptr_t)b0 - (intptr_t)w0) / 4;
             }
           }
-          d.row = row;
-          d.slice = slice;
-          d.mode = mode;
-          d.nb = nb;
-          d.hcount = pen ? H : 0;
-          d.hb = h0;
-          d.hlead = hlead;
-          d.hbn = hbn;
-          d.T = T;
-          d.mp = mp;
-          d.rep = rp;
-          d.freq = fq;
-          d.pres = pr;
-          d.k = k;
-          mbar_expect_tx(&ctl->full[s], (uint32_t)(nb + hbn * 4));
-          unsigned char* dst = smem + s * stage_bytes;
-          constexpr int CH = 32768;
-          for (int off = 0; off < nb; off += CH)
-            bulk_g2s(dst + off, g0 + off, (uint32_t)min(CH, nb - off), &ctl->full[s]);
-          if (hbn > 0)
-            bulk_g2s(dst + a.tile_bytes, reinterpret_cast<const void*>(w0), (uint32_t)(hbn * 4), &ctl->full[s]);
+          nd.row = row;
+          nd.slice = slice;
+          nd.mode = mode;
+          nd.nb = nb;
+          nd.hcount = pen ? H : 0;
+          nd.hb = h0;
+          nd.hlead = hlead;
+          nd.hbn = hbn;
+          nd.T = T;
+          nd.rep = rp;
+          nd.freq = fq;
+          nd.pres = pr;
+          nd.k = (k > 0 && k < V) ? k : 0;
+          nd.lo = lo;
+          nd.n = n;
+          nd.tl = (mp > 0.0f && mp < 1.0f) ? __fmul_rn(T, logf(mp)) : 0.0f;
+          nd.sb = __fdiv_rn(BIN_PER_NAT, T);
+          nd.binw = __fdiv_rn(T, BIN_PER_NAT);
         }
+        if (j >= 2 && !mbar_wait_bounded_sleep(&ctl->empty[s], (uint32_t)(((j >> 1) - 1) & 1)))
+          atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
+        ctl->desc[s] = nd;
+        mbar_expect_tx(&ctl->full[s], (uint32_t)(nd.nb + nd.hbn * 4));
+        unsigned char* dst = smem + s * stage_bytes;
+        constexpr int CH = 32768;
+        for (int off = 0; off < nd.nb; off += CH)
+          bulk_g2s(dst + off, g0 + off, (uint32_t)min(CH, nd.nb - off), &ctl->full[s]);
+        if (nd.hbn > 0)
+          bulk_g2s(dst + a.tile_bytes, reinterpret_cast<const void*>(w0), (uint32_t)(nd.hbn * 4), &ctl->full[s]);
       }
       __syncwarp();
       if (t >= nitems) break;
@@ -229,7 +249,12 @@ __global__ void __launch_bounds__(NT, 1) lss_scan_kernel(const ScanArgs a) {
   }
 
   // =======================================================================================
-  // Compute warps
+  // Compute warps.  Item j runs in two phases separated by barriers:
+  //   M(j): the slice into registers with the history penalties applied, the slice max,
+  //         then the release of the stage;
+  //   X(j): the threshold, the candidates and the summary.
+  // The preparation of item j + 1 (what the bulk copy skipped, 16-bit widening, padding and
+  // the history counts) follows X(j) directly, so warps that finish X(j) early overlap it.
   // =======================================================================================
   const int ctid = tid;  // 0 .. SC_CT-1
   auto load_elem = [&](const char* g0, int i) -> float {
@@ -237,280 +262,302 @@ __global__ void __launch_bounds__(NT, 1) lss_scan_kernel(const ScanArgs a) {
     if (DT == LSS_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(g0)[i]);
     return __half2float(reinterpret_cast<const __half*>(g0)[i]);
   };
+  bool wrote = false;  // this thread wrote the stage through the generic proxy
+  // Waits for item jj's stage and prepares it; false at the end of the list (uniform).
+  auto prepare = [&](int jj) -> bool {
+    const int s = jj & 1;
+    if (!mbar_wait_bounded_sleep(&ctl->full[s], (uint32_t)((jj >> 1) & 1)) && ctid == 0)
+      atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
+    const ItemDesc& D = ctl->desc[s];
+    const int mode = D.mode;
+    wrote = false;
+    if (mode == ITEM_END) return false;
+    if (mode == ITEM_SKIP) return true;
+    const int row = D.row, lo = D.lo, n = D.n;
+    const int n4 = (n + 3) >> 2;
+    float* tile = reinterpret_cast<float*>(smem + s * stage_bytes);
+    const char* g0 = reinterpret_cast<const char*>(a.logits) + ((int64_t)row * a.row_stride + lo) * ES;
+    const int nbulk = D.nb / ES;
+    // ---- what the bulk copy skipped (ragged tail / unaligned rows), widening, padding
+    float tailv = 0.0f;
+    const int ntail = n - nbulk;
+    if (DT == LSS_DTYPE_F32 || nbulk == 0) {
+      for (int i = nbulk + ctid; i < n; i += SC_CT) {
+        tile[i] = load_elem(g0, i);
+        wrote = true;
+      }
+    } else if (ctid < ntail) {
+      tailv = load_elem(g0, nbulk + ctid);
+    }
+    if (DT != LSS_DTYPE_F32 && nbulk > 0) {
+      // Widen in place, back to front: chunk c's f32 writes only overwrite 16-bit data of
+      // chunks >= 2c, which earlier iterations consumed.
+      const uint16_t* h = reinterpret_cast<const uint16_t*>(tile);
+      constexpr int W = SC_CT * 8;
+      const int nch = (nbulk + W - 1) / W;
+      for (int c = nch - 1; c >= 0; --c) {
+        const int i0 = c * W + ctid * 8;
+        float v[8];
+        const bool act = i0 < nbulk;
+        if (act) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(h + i0);
+          const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (DT == LSS_DTYPE_BF16) {
+              v[2 * q] = __uint_as_float(w[q] << 16);
+              v[2 * q + 1] = __uint_as_float(w[q] & 0xffff0000u);
+            } else {
+              v[2 * q] = __half2float(__ushort_as_half((uint16_t)(w[q] & 0xffffu)));
+              v[2 * q + 1] = __half2float(__ushort_as_half((uint16_t)(w[q] >> 16)));
+            }
+          }
+        }
+        sc_sync();
+        if (act) {
+          float4* dd = reinterpret_cast<float4*>(tile + i0);
+          dd[0] = make_float4(v[0], v[1], v[2], v[3]);
+          dd[1] = make_float4(v[4], v[5], v[6], v[7]);
+          wrote = true;
+        }
+      }
+      sc_sync();
+      if (ctid < ntail) tile[nbulk + ctid] = tailv;
+    }
+    if (ctid < n4 * 4 - n) {
+      tile[n + ctid] = -INFINITY;
+      wrote = true;
+    }
+    // ---- history ids in the slice counted (one shared add per occurrence, no return value)
+    const int H = D.hcount;
+    if (H > 0 && H <= SC_HMAX) {
+      const int32_t* hs = reinterpret_cast<const int32_t*>(smem + s * stage_bytes + a.tile_bytes);
+      const int hlead = D.hlead, hbn = D.hbn, hb = D.hb;
+      constexpr int HU = 3;
+      for (int j0 = 0; j0 < H; j0 += SC_CT * HU) {
+        int idl[HU];
+#pragma unroll
+        for (int u = 0; u < HU; ++u) {
+          const int jj2 = j0 + u * SC_CT + ctid;
+          idl[u] = -1;
+          if (jj2 < H) {
+            const int w = jj2 + hlead;
+            const int raw = (w >= 0 && w < hbn) ? hs[w] : a.hist_ids[hb + jj2];
+            if ((unsigned)raw >= (unsigned)V) atomicOr(a.err, LSS_FLAG_BAD_HISTORY);
+            else if ((unsigned)(raw - lo) < (unsigned)n) idl[u] = raw - lo;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < HU; ++u)
+          if (idl[u] >= 0) atomicAdd(&hcnt2[idl[u] >> 1], 1u << ((idl[u] & 1) << 4));
+      }
+    }
+    return true;
+  };
+
+  // Summary of the previous item, written by warp 0 once the barrier that opens the next item
+  // shows every warp done with it.
+  int pmode = ITEM_SKIP, prow = 0, pslice = 0, ps = 0;
+  uint32_t pkey = 0;
+  auto write_summary = [&]() {  // warp 0
+    if (pmode == ITEM_SKIP) return;
+    uint64_t av = pkey;
+    if (pmode == ITEM_GREEDY) {
+      uint64_t b = lane < SC_CW ? ctl->best[ps][lane] : 0ull;
+      av = warp_allreduce(b, MaxU64());
+    }
+    if (lane == 0) {
+      ItemScratch* q = &ctl->sc[ps];
+      a.summ[(int64_t)prow * S + pslice] = make_uint4((uint32_t)av, (uint32_t)(av >> 32), q->cnt, q->flags);
+      q->cnt = 0u;
+      q->flags = 0u;
+    }
+  };
+
+  if (!prepare(0)) return;
   for (int j = 0;; ++j) {
     const int s = j & 1;
-    if (!mbar_wait_bounded(&ctl->full[s], (uint32_t)((j >> 1) & 1)) && ctid == 0)
-      atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
-    const ItemDesc d = ctl->desc[s];
-    if (d.mode == ITEM_END) break;
     ItemScratch* sc = &ctl->sc[s];
-    if (d.mode != ITEM_SKIP) {
-      const int row = d.row, lo = d.slice * TS;
-      const int n = min(V, lo + TS) - lo;
-      const int n4 = (n + 3) >> 2;
-      float* tile = reinterpret_cast<float*>(smem + s * stage_bytes);
-      const float4* t4 = reinterpret_cast<const float4*>(tile);
-      const char* g0 = reinterpret_cast<const char*>(a.logits) + ((int64_t)row * a.row_stride + lo) * ES;
-      const int nbulk = d.nb / ES;
+    const ItemDesc& D = ctl->desc[s];
+    sc_sync();  // item j: slice and history counts complete; item j-1 done by every warp
+    if (warp == 0) write_summary();
+    const int mode = D.mode;
+    const int lo = D.lo, n = D.n, n4 = (n + 3) >> 2;
+    const float4* t4 = reinterpret_cast<const float4*>(smem + s * stage_bytes);
+    const int k = D.k;
+    float4 v[SC_R];
+    float tmax = -INFINITY;  // max of this thread's values
 
-      // ---- the slice: plain loads of what the bulk copy skipped, 16-bit widening, padding
-      float tailv = 0.0f;
-      const int ntail = n - nbulk;
-      if (DT == LSS_DTYPE_F32 || nbulk == 0) {
-        for (int i = nbulk + ctid; i < n; i += SC_CT) tile[i] = load_elem(g0, i);
-      } else if (ctid < ntail) {
-        tailv = load_elem(g0, nbulk + ctid);
-      }
-      if (DT != LSS_DTYPE_F32 && nbulk > 0) {
-        // Widen in place, back to front: chunk c's f32 writes only overwrite 16-bit data of
-        // chunks >= 2c, which earlier iterations consumed.
-        const uint16_t* h = reinterpret_cast<const uint16_t*>(tile);
-        constexpr int W = SC_CT * 8;
-        const int nch = (nbulk + W - 1) / W;
-        for (int c = nch - 1; c >= 0; --c) {
-          const int i0 = c * W + ctid * 8;
-          float v[8];
-          const bool act = i0 < nbulk;
-          if (act) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(h + i0);
-            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    // ---- M(j)
+    if (mode == ITEM_GREEDY) {
+      // Greedy row (sampling.py:132-133): argmax of the raw slice, NaN first.
+      uint64_t best = 0;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              if (DT == LSS_DTYPE_BF16) {
-                v[2 * q] = __uint_as_float(w[q] << 16);
-                v[2 * q + 1] = __uint_as_float(w[q] & 0xffff0000u);
-              } else {
-                v[2 * q] = __half2float(__ushort_as_half((uint16_t)(w[q] & 0xffffu)));
-                v[2 * q + 1] = __half2float(__ushort_as_half((uint16_t)(w[q] >> 16)));
-              }
+      for (int i = 0; i < SC_R; ++i) {
+        const int q = i * SC_CT + ctid;
+        if (q < n4) {
+          const float4 x = t4[q];
+          const int ix = lo + 4 * q;
+          best = max(best, argmax_code(x.x, ix));
+          best = max(best, argmax_code(x.y, ix + 1));
+          best = max(best, argmax_code(x.z, ix + 2));
+          best = max(best, argmax_code(x.w, ix + 3));
+        }
+      }
+      best = warp_allreduce(best, MaxU64());
+      if (lane == 0) ctl->best[s][warp] = best;
+    } else if (mode == ITEM_SAMPLE) {
+      // Penalties (sampling.py:55-66) once per unique id, from the counters of the thread's
+      // own entries, which it resets; then the slice max of z.
+      const int H = D.hcount;
+      const bool pen = H > 0 && H <= SC_HMAX;
+      float4* t4w = reinterpret_cast<float4*>(smem + s * stage_bytes);
+#pragma unroll
+      for (int i = 0; i < SC_R; ++i) {
+        const int q = i * SC_CT + ctid;
+        v[i] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        if (q < n4) {
+          if (pen) {
+            uint2* cp = reinterpret_cast<uint2*>(hcnt2 + 2 * q);
+            const uint2 c = *cp;
+            if ((c.x | c.y) != 0u) {
+              apply4(t4w + q, c, D.rep, D.freq, D.pres);
+              *cp = make_uint2(0u, 0u);
+              wrote = true;
             }
           }
-          sc_sync();
-          if (act) {
-            float4* dd = reinterpret_cast<float4*>(tile + i0);
-            dd[0] = make_float4(v[0], v[1], v[2], v[3]);
-            dd[1] = make_float4(v[4], v[5], v[6], v[7]);
-          }
+          v[i] = t4[q];
         }
-        sc_sync();
-        if (ctid < ntail) tile[nbulk + ctid] = tailv;
+        tmax = fmax_nan(tmax, fmax_nan(fmax_nan(v[i].x, v[i].y), fmax_nan(v[i].z, v[i].w)));
       }
-      if (ctid < n4 * 4 - n) tile[n + ctid] = -INFINITY;
+      const float wmax = warp_allreduce(tmax, MaxF());
+      if (lane == 0) ctl->wkey[s][warp] = (!(wmax == wmax) || wmax == INFINITY) ? 0xffffffffu : f2key(wmax);
+      if (H > SC_HMAX && ctid == 0) atomicOr(&sc->flags, SUM_HASH);  // counts not kept
+      if (k)
+        for (int i = ctid; i < NBIN + 1; i += SC_CT) HL[i] = 0u;
+    }
+    // The values sit in registers: what X needs of the descriptor is copied out and the
+    // stage released, so that the next copy into it starts now.
+    const int row = D.row, slice = D.slice;
+    const float T = D.T, tl = D.tl, sbin = D.sb, binw = D.binw;
+    if (wrote) fence_proxy_async();  // generic writes to the stage precede the next bulk copy
+    __syncwarp();
+    if (lane == 0) mbar_arrive_local(&ctl->empty[s]);
+    sc_sync();
 
-      // ---- history ids of this slice into the hash (one atomic per distinct id per warp)
-      const bool pen = d.hcount > 0;
-      if (pen) {
-        const int32_t* hs = reinterpret_cast<const int32_t*>(smem + s * stage_bytes + a.tile_bytes);
-        const int H = d.hcount;
-        for (int j0 = 0; j0 < H; j0 += SC_CT) {  // warp-uniform trip count
-          const int jj = j0 + ctid;
-          int id = -1;
-          if (jj < H) {
-            const int w = jj + d.hlead;
-            const int raw = (w >= 0 && w < d.hbn) ? hs[w] : a.hist_ids[d.hb + jj];
-            if (raw < 0 || raw >= V) atomicOr(a.err, LSS_FLAG_BAD_HISTORY);
-            else if (raw >= lo && raw < lo + n) id = raw - lo;
-          }
-          if (__ballot_sync(0xffffffffu, id >= 0)) {
-            const unsigned same = __match_any_sync(0xffffffffu, id);
-            if (id >= 0 && lane == __ffs(same) - 1) {
-              uint32_t hh = ((uint32_t)id * 2654435761u) >> SC_HSHIFT;
-              bool placed = false;
-              for (int probe = 0; probe < SC_HSLOTS; ++probe) {
-                const uint32_t old = atomicCAS(&hkeys[hh], HASH_EMPTY, (uint32_t)id);
-                if (old == HASH_EMPTY) hlist[atomicAdd(&sc->nslots, 1u)] = (uint16_t)hh;
-                if (old == HASH_EMPTY || old == (uint32_t)id) {
-                  atomicAdd(&hcnts[hh], (uint32_t)__popc(same));
-                  placed = true;
-                  break;
-                }
-                hh = (hh + 1) & (SC_HSLOTS - 1);
-              }
-              if (!placed) atomicOr(&sc->flags, SUM_HASH);
-            }
-          }
-        }
-      }
-      sc_sync();  // slice complete, hash built
-      if (pen) {
-        // Penalties once per unique id; the slots used are emptied for the next item.
-        const uint32_t ns = *reinterpret_cast<volatile uint32_t*>(&sc->nslots);
-        for (uint32_t i = ctid; i < ns; i += SC_CT) {
-          const uint32_t hh = hlist[i];
-          const uint32_t id = hkeys[hh];
-          tile[id] = penalise(tile[id], d.rep, d.freq, d.pres, (int)hcnts[hh]);
-          hkeys[hh] = HASH_EMPTY;
-          hcnts[hh] = 0;
-        }
-        sc_sync();
-      }
-
-      if (d.mode == ITEM_GREEDY) {
-        // ---- greedy row (sampling.py:132-133): argmax of the raw slice, NaN first
-        uint64_t best = 0;
-#pragma unroll
-        for (int i = 0; i < SC_R; ++i) {
-          const int q = i * SC_CT + ctid;
-          if (q < n4) {
-            const float4 v = t4[q];
-            const int ix = lo + 4 * q;
-            best = max(best, argmax_code(v.x, ix));
-            best = max(best, argmax_code(v.y, ix + 1));
-            best = max(best, argmax_code(v.z, ix + 2));
-            best = max(best, argmax_code(v.w, ix + 3));
-          }
-        }
-        best = warp_allreduce(best, MaxU64());
-        if (lane == 0) atomicMax(&sc->best, (unsigned long long)best);
-      } else {
-        // ---- slice max of z, values kept in registers
-        float4 v[SC_R];
-        float wmax = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < SC_R; ++i) {
-          const int q = i * SC_CT + ctid;
-          v[i] = q < n4 ? t4[q] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-          wmax = fmax_nan(wmax, fmax_nan(fmax_nan(v[i].x, v[i].y), fmax_nan(v[i].z, v[i].w)));
-        }
-        wmax = warp_allreduce(wmax, MaxF());
-        if (lane == 0) {
-          if (!(wmax == wmax) || wmax == INFINITY) atomicOr(&sc->flags, SUM_SPECIAL);
-          else atomicMax(&sc->maxk, f2key(wmax));
-        }
-        const float T = d.T, mp = d.mp;
-        const int k = d.k;
-        const bool tk_on = k > 0 && k < V;
-        const bool mp_on = mp > 0.0f && mp < 1.0f;
-        if (tk_on)
-          for (int i = ctid; i < NBIN + 1; i += SC_CT) HL[i] = 0u;
-        sc_sync();
-        const bool special = (*reinterpret_cast<volatile uint32_t*>(&sc->flags) & SUM_SPECIAL) != 0u;
-        const float M = key2f(*reinterpret_cast<volatile uint32_t*>(&sc->maxk));
-        const float my = __fdiv_rn(M, T);
-        float thr = INFINITY;  // candidates: z >= thr
-        if (!special && my == INFINITY) {
-          if (lane == 0 && warp == 0) atomicOr(&sc->flags, SUM_SPECIAL);  // y overflows
-        } else if (!special && M > -INFINITY) {
-          const float zmp = mp_on ? z_floor_for(minp_floor_y(my, mp), T) : -INFINITY;
-          if (tk_on) {
-            // Count histogram of z over the slice (bins of 1/16 nat of y below the slice
-            // max, values above the min-p floor), then the bin of the slice's k-th largest.
-            const float sb = __fdiv_rn(BIN_PER_NAT, T);
-            uint32_t far_c = 0;
-#pragma unroll
-            for (int i = 0; i < SC_R; ++i) {
-              const float zs[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                if (!(zs[q] >= zmp) || zs[q] == -INFINITY) continue;
-                const float dd = __fmul_rn(__fsub_rn(M, zs[q]), sb);
-                if (dd < (float)NBIN) atomicAdd(&HL[(int)dd], 1u); else far_c++;
-              }
-            }
-            far_c = warp_allreduce(far_c, SumU32());
-            if (lane == 0 && far_c) atomicAdd(&HL[NBIN], far_c);
-            sc_sync();
-            // Every warp scans the bins (lane l holds bins 8l .. 8l+7).
-            uint32_t c8[8];
-            uint32_t loc = 0;
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              c8[q] = HL[8 * lane + q];
-              loc += c8[q];
-            }
-            uint32_t incl = loc;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-              const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-              if (lane >= o) incl += y;
-            }
-            const unsigned hit = __ballot_sync(0xffffffffu, incl >= (uint32_t)k);
-            int bk = NBIN;
-            if (hit) {
-              const int L = __ffs(hit) - 1;
-              int b = 0;
-              uint32_t acc = incl - loc;
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                acc += c8[q];
-                if (acc < (uint32_t)k) b = q + 1;
-              }
-              bk = __shfl_sync(0xffffffffu, 8 * lane + b, L);
-            }
-            const uint32_t total = __shfl_sync(0xffffffffu, incl, 31) + HL[NBIN];
-            if (bk < NBIN) {
-              // Two bins of slack below the k-th largest cover values whose y ties with it.
-              float zw = __fsub_rn(M, __fdiv_rn((float)(bk + 2), sb));
-              zw = __fsub_rn(zw, fabsf(zw) * 2.384185791015625e-07f + 1e-37f);
-              thr = fmaxf(zw, zmp);
-            } else if (total > (uint32_t)k) {
-              if (lane == 0 && warp == 0) atomicOr(&sc->flags, SUM_FAR);  // k-th largest > 16 nats down
-            } else {
-              thr = mp_on ? zmp : -FLT_MAX;  // fewer than k values: every finite value above the floor
-            }
-          } else if (mp_on) {
-            thr = zmp;
-          } else {
-            thr = -FLT_MAX;  // small vocabulary: every finite value is a candidate
-          }
-        }
-        // ---- candidates into the item's segment
-        if (thr < INFINITY) {
-          uint64_t* out = a.cand + ((int64_t)row * S + d.slice) * a.SEG;
-          const uint32_t SEG = (uint32_t)a.SEG;
+    // ---- X(j)
+    uint32_t mk = 0;
+    if (mode == ITEM_SAMPLE) {
+      mk = lane < SC_CW ? ctl->wkey[s][lane] : 0u;
+      mk = warp_allreduce(mk, MaxU32());
+      const bool special = mk == 0xffffffffu;
+      if (special && ctid == 0) atomicOr(&sc->flags, SUM_SPECIAL);
+      const float M = key2f(mk);
+      float thr = INFINITY;  // candidates: z >= thr
+      if (!special && M > -INFINITY) {
+        // Min-p floor in z: exp(y - max) >= p  <=>  z >= max_z + T ln p (y = z / T), less a
+        // margin of 2^-11 relative that covers every rounding of the exact filter.
+        const float zmp = tl != 0.0f ? __fsub_rn(__fadd_rn(M, tl), (fabsf(M) + fabsf(tl) + T) * 4.8828125e-04f)
+                                     : -INFINITY;
+        if (k) {
+          // Count histogram of z over the slice (bins of 1/16 nat of y below the slice max,
+          // values above the min-p floor), then the bin of the slice's k-th largest.
+          uint32_t far_c = 0;
 #pragma unroll
           for (int i = 0; i < SC_R; ++i) {
-            const bool any = v[i].x >= thr || v[i].y >= thr || v[i].z >= thr || v[i].w >= thr;
-            if (__ballot_sync(0xffffffffu, any) == 0u) continue;
-            const int q = i * SC_CT + ctid;
             const float zs[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const bool keep = zs[c] >= thr;
-              const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-              if (bal) {
-                const int leader = __ffs(bal) - 1;
-                uint32_t base = 0;
-                if (lane == leader) base = atomicAdd(&sc->cnt, (uint32_t)__popc(bal));
-                base = __shfl_sync(0xffffffffu, base, leader);
-                if (keep) {
-                  const uint32_t pos = base + __popc(bal & ((1u << lane) - 1u));
-                  if (pos < SEG) out[pos] = ((uint64_t)f2key(zs[c]) << 32) | (uint32_t)(~(uint32_t)(lo + 4 * q + c));
-                }
+            for (int q = 0; q < 4; ++q) {
+              if (!(zs[q] >= zmp) || zs[q] == -INFINITY) continue;
+              const float dd = __fmul_rn(__fsub_rn(M, zs[q]), sbin);
+              if (dd < (float)NBIN) atomicAdd(&HL[(int)dd], 1u); else far_c++;
+            }
+          }
+          far_c = warp_allreduce(far_c, SumU32());
+          if (lane == 0 && far_c) atomicAdd(&HL[NBIN], far_c);
+          sc_sync();
+          // Every warp scans the bins (lane l holds bins 8l .. 8l+7).
+          uint32_t c8[8];
+          uint32_t loc = 0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            c8[q] = HL[8 * lane + q];
+            loc += c8[q];
+          }
+          uint32_t incl = loc;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+          }
+          const unsigned hit = __ballot_sync(0xffffffffu, incl >= (uint32_t)k);
+          int bk = NBIN;
+          if (hit) {
+            const int L = __ffs(hit) - 1;
+            int b = 0;
+            uint32_t acc = incl - loc;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              acc += c8[q];
+              if (acc < (uint32_t)k) b = q + 1;
+            }
+            bk = __shfl_sync(0xffffffffu, 8 * lane + b, L);
+          }
+          const uint32_t total = __shfl_sync(0xffffffffu, incl, 31) + HL[NBIN];
+          if (bk < NBIN) {
+            // The k-th largest lies in bin bk: (max - z_k) * sb < bk + 1.  One more bin of
+            // slack covers the rounding of the bins and values whose y ties with it.
+            float zw = __fsub_rn(M, __fmul_rn((float)(bk + 2), binw));
+            zw = __fsub_rn(zw, fabsf(zw) * 2.384185791015625e-07f + 1e-37f);
+            thr = fmaxf(zw, zmp);
+          } else if (total > (uint32_t)k) {
+            if (ctid == 0) atomicOr(&sc->flags, SUM_FAR);  // the k-th largest lies > 16 nats down
+          } else {
+            thr = tl != 0.0f ? zmp : -FLT_MAX;  // fewer than k values: every finite value above the floor
+          }
+        } else if (tl != 0.0f) {
+          thr = zmp;
+        } else {
+          thr = -FLT_MAX;  // small vocabulary: every finite value is a candidate
+        }
+      }
+      // ---- candidates into the item's segment
+      if (__ballot_sync(0xffffffffu, tmax >= thr) != 0u) {
+        uint64_t* out = a.cand + ((int64_t)row * S + slice) * a.SEG;
+        const uint32_t SEG = (uint32_t)a.SEG;
+#pragma unroll
+        for (int i = 0; i < SC_R; ++i) {
+          const bool any = v[i].x >= thr || v[i].y >= thr || v[i].z >= thr || v[i].w >= thr;
+          if (__ballot_sync(0xffffffffu, any) == 0u) continue;
+          const int q = i * SC_CT + ctid;
+          const float zs[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const bool keep = zs[c] >= thr;
+            const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+            if (bal) {
+              const int leader = __ffs(bal) - 1;
+              uint32_t base = 0;
+              if (lane == leader) base = atomicAdd(&sc->cnt, (uint32_t)__popc(bal));
+              base = __shfl_sync(0xffffffffu, base, leader);
+              if (keep) {
+                const uint32_t pos = base + __popc(bal & ((1u << lane) - 1u));
+                if (pos < SEG) out[pos] = ((uint64_t)f2key(zs[c]) << 32) | (uint32_t)(~(uint32_t)(lo + 4 * q + c));
               }
             }
           }
         }
       }
     }
-    // ---- release the stage; the last warp of the item writes its summary
-    fence_proxy_async();  // this warp's accesses to the stage precede the next bulk copy
-    __syncwarp();
-    if (lane == 0) {
-      if (d.mode != ITEM_SKIP) {
-        __threadfence_block();
-        const uint32_t prev = atomicAdd(&sc->done, 1u);
-        if (prev == (uint32_t)(SC_CW - 1)) {
-          __threadfence_block();
-          volatile ItemScratch* vs = sc;
-          const uint64_t av = d.mode == ITEM_GREEDY ? (uint64_t)vs->best : (uint64_t)vs->maxk;
-          uint4 sm;
-          sm.x = (uint32_t)av;
-          sm.y = (uint32_t)(av >> 32);
-          sm.z = vs->cnt;
-          sm.w = vs->flags;
-          a.summ[(int64_t)d.row * S + d.slice] = sm;
-          vs->best = 0ull;
-          vs->maxk = 0u;
-          vs->flags = 0u;
-          vs->cnt = 0u;
-          vs->nslots = 0u;
-          vs->done = 0u;
-        }
-      }
-      mbar_arrive_local(&ctl->empty[s]);
-    }
+    pmode = mode;
+    prow = row;
+    pslice = slice;
+    ps = s;
+    pkey = mk;
+    if (!prepare(j + 1)) break;
   }
+  sc_sync();
+  if (warp == 0) write_summary();
 }
 
 }  // namespace lss
