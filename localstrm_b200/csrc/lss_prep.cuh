@@ -1,10 +1,12 @@
-// lss_prep.cuh — history preparation of one row for the second kernel.
+// lss_prep.cuh — history preparation: the history of a row as unique (id, count) pairs
+// (torch.unique of the history, sampling.py:52), grouped by vocabulary slice.
 //
-// The history of a non-greedy row with an active penalty becomes unique (id, count) pairs
-// (torch.unique, sampling.py:52), grouped by the CTA slice [c*TE, (c+1)*TE) that holds the id,
-// so that each CTA of the row's cluster applies only its own segment.  One CTA does the whole
-// row: histories of up to PREP_SMEM_SLOTS / 2 ids hash in the shared memory handed in, longer
-// ones in a global table of 2H slots.
+// prep_row does one row with the whole CTA: histories of up to PREP_SMEM_SLOTS / 2 ids hash
+// in the shared memory handed in, longer ones in a global table of 2H slots.  The pairs of
+// slice c ([c*TE, (c+1)*TE)) land in uniq_ids / uniq_cnt[hist_off[row] + so[c] ..
+// hist_off[row] + so[c+1]).  K0, lss_hist_kernel, runs it for every row with the scan
+// kernel's slices; the second kernel runs it again for the rows it takes, with its own
+// slices.
 #pragma once
 
 #include "lss_common.cuh"
@@ -12,20 +14,29 @@
 namespace lss {
 
 constexpr int PREP_SMEM_SLOTS = 4096;   // histories up to 2,048 ids hash in shared memory
+constexpr int PREP_MAXSEG = 32;         // slices per row
 constexpr uint32_t EMPTY = 0xffffffffu;
 
-// `skeys` / `scnts`: PREP_SMEM_SLOTS words each; `bcnt` MAXCL + 1 words, `bfill` MAXCL words.
-// Writes uniq_ids / uniq_cnt at hist_off[row] + ... and seg_off[row][0 .. MAXCL].
-__device__ void prep_row(const RowArgs& a, int row, int TE, int CL, uint32_t* skeys, uint32_t* scnts,
-                         uint32_t* bcnt, uint32_t* bfill) {
+struct PrepOut {
+  int32_t* so;         // this row's segment offsets, nseg + 1 entries
+  uint32_t* bad;       // OR'ed with LSS_FLAG_BAD_HISTORY for an id outside [0, V)
+};
+
+// Whole CTA (NTH threads, `sync` its barrier).  `skeys` / `scnts`: PREP_SMEM_SLOTS words each;
+// `bcnt`: PREP_MAXSEG + 1 words, `bfill`: PREP_MAXSEG words.  `active`: the row's penalties
+// apply (otherwise only empty segments are written).
+template <int NTH, class Sync>
+__device__ void prep_row(const RowArgs& a, int row, bool active, int TE, int nseg, const PrepOut& o,
+                         uint32_t* skeys, uint32_t* scnts, uint32_t* bcnt, uint32_t* bfill, Sync sync) {
   const int tid = threadIdx.x, lane = tid & 31;
-  int32_t* so = a.seg_off + (int64_t)row * (MAXCL + 1);
-  const float T = a.temperature[row];
+  if (!active) {
+    if (tid <= nseg) o.so[tid] = 0;
+    return;
+  }
   const int b = a.hist_off[row], e = a.hist_off[row + 1];
   const int H = e - b;
-  const bool active = T > 0.0f && H > 0 && (a.rep[row] != 1.0f || a.freq[row] != 0.0f || a.pres[row] != 0.0f);
-  if (!active) {
-    if (tid <= MAXCL) so[tid] = 0;
+  if (H <= 0) {
+    if (tid <= nseg) o.so[tid] = 0;
     return;
   }
   uint32_t *keys, *cnts;
@@ -42,28 +53,28 @@ __device__ void prep_row(const RowArgs& a, int row, int TE, int CL, uint32_t* sk
     cnts = a.gcnts + 2 * (int64_t)b;
     pow2 = false;
   }
-  for (uint32_t s = tid; s < cap; s += NT) {
+  for (uint32_t s = tid; s < cap; s += NTH) {
     keys[s] = EMPTY;
     cnts[s] = 0;
   }
-  if (tid <= MAXCL) bcnt[tid] = 0;
-  if (tid < MAXCL) bfill[tid] = 0;
-  __syncthreads();
+  if (tid <= PREP_MAXSEG) bcnt[tid] = 0;
+  if (tid < PREP_MAXSEG) bfill[tid] = 0;
+  sync();
   // Insert: lanes holding the same id are merged first (one atomic per distinct id per warp).
-  // Eight ids per thread are loaded before any is inserted, so their latencies overlap.
+  // U ids per thread are loaded before any is inserted, so their latencies overlap.
   constexpr int U = 8;
-  for (int j0 = 0; j0 < H; j0 += NT * U) {
+  for (int j0 = 0; j0 < H; j0 += NTH * U) {
     int idv[U];
 #pragma unroll
     for (int t = 0; t < U; ++t) {
-      const int j = j0 + t * NT + tid;
+      const int j = j0 + t * NTH + tid;
       idv[t] = j < H ? a.hist_ids[b + j] : INT32_MIN;  // INT32_MIN: no entry
     }
 #pragma unroll
     for (int t = 0; t < U; ++t) {
       int id = idv[t] == INT32_MIN ? -1 : idv[t];
       if (idv[t] != INT32_MIN && (id < 0 || id >= a.V)) {
-        atomicOr(a.err, LSS_FLAG_BAD_HISTORY);
+        atomicOr(o.bad, LSS_FLAG_BAD_HISTORY);
         id = -1;
       }
       const unsigned same = __match_any_sync(0xffffffffu, id);
@@ -81,26 +92,26 @@ __device__ void prep_row(const RowArgs& a, int row, int TE, int CL, uint32_t* sk
       }
     }
   }
-  __syncthreads();
-  // Group by CTA slice: count, exclusive scan, scatter (one atomic per slice per warp).
-  for (uint32_t s0 = 0; s0 < cap; s0 += NT) {
+  sync();
+  // Group by slice: count, exclusive scan, scatter (one atomic per slice per warp).
+  for (uint32_t s0 = 0; s0 < cap; s0 += NTH) {
     const uint32_t s = s0 + tid;
     const uint32_t k = s < cap ? keys[s] : EMPTY;
     const int c = k != EMPTY ? (int)(k / (uint32_t)TE) : -1;
     const unsigned same = __match_any_sync(0xffffffffu, c);
     if (c >= 0 && lane == __ffs(same) - 1) atomicAdd(&bcnt[c], (uint32_t)__popc(same));
   }
-  __syncthreads();
+  sync();
   if (tid == 0) {
     uint32_t run = 0;
-    for (int c = 0; c <= MAXCL; ++c) {
-      const uint32_t v = c < CL ? bcnt[c] : 0u;
+    for (int c = 0; c <= PREP_MAXSEG; ++c) {
+      const uint32_t v = c < nseg ? bcnt[c] : 0u;
       bcnt[c] = run;
       run += v;
     }
   }
-  __syncthreads();
-  for (uint32_t s0 = 0; s0 < cap; s0 += NT) {
+  sync();
+  for (uint32_t s0 = 0; s0 < cap; s0 += NTH) {
     const uint32_t s = s0 + tid;
     const uint32_t k = s < cap ? keys[s] : EMPTY;
     const int c = k != EMPTY ? (int)(k / (uint32_t)TE) : -1;
@@ -115,7 +126,46 @@ __device__ void prep_row(const RowArgs& a, int row, int TE, int CL, uint32_t* sk
       a.uniq_cnt[b + pos] = (int32_t)cnts[s];
     }
   }
-  if (tid <= MAXCL) so[tid] = (int32_t)bcnt[tid <= CL ? tid : CL];
+  if (tid <= nseg) o.so[tid] = (int32_t)bcnt[tid];
+}
+
+struct BlockSync {
+  __device__ void operator()() const { __syncthreads(); }
+};
+
+// =========================================================================================
+// K0: history kernel — one CTA per row: the (id, count) pairs of the rows whose penalties
+// the scan kernel applies, grouped by its slices (seg2[row][0 .. S]); a per-row flag for ids
+// outside [0, V).  Block 0 clears the workspace status first (no other block writes it).
+// =========================================================================================
+constexpr int HIST_NT = 512;
+
+struct HistArgs {
+  RowArgs r;
+  int S, TS;
+  int32_t* seg2;        // [B][S + 1]
+  uint32_t* rowflag;    // [B]
+  uint32_t* header;     // 64 words
+};
+
+__global__ void __launch_bounds__(HIST_NT) lss_hist_kernel(const HistArgs h) {
+  __shared__ uint32_t skeys[PREP_SMEM_SLOTS];
+  __shared__ uint32_t scnts[PREP_SMEM_SLOTS];
+  __shared__ uint32_t bcnt[PREP_MAXSEG + 1];
+  __shared__ uint32_t bfill[PREP_MAXSEG];
+  const RowArgs& a = h.r;
+  const int row = blockIdx.x;
+  if (row == 0 && threadIdx.x < 64) h.header[threadIdx.x] = 0u;
+  if (threadIdx.x == 0) h.rowflag[row] = 0u;
+  const float T = a.temperature[row];
+  const int k = a.top_k[row];
+  const float mp = a.min_p[row];
+  const bool bounded = (k > 0 && k < a.V) || (mp > 0.0f && mp < 1.0f) || a.V <= FAST_CAP / 2;
+  const bool active = a.use_hist && T > 0.0f && bounded &&
+                      (a.rep[row] != 1.0f || a.freq[row] != 0.0f || a.pres[row] != 0.0f);
+  __syncthreads();
+  const PrepOut o{h.seg2 + (int64_t)row * (h.S + 1), h.rowflag + row};
+  prep_row<HIST_NT>(a, row, active, h.TS, h.S, o, skeys, scnts, bcnt, bfill, BlockSync());
 }
 
 }  // namespace lss

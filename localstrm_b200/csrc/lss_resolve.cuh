@@ -194,9 +194,10 @@ __device__ void resolve_warp(uint64_t v, int nc, const ResolveIn& in, const RowA
 // history overflow the fixed buffers go to the deferred list for the second kernel.
 // =========================================================================================
 struct GatherArgs {
-  const uint4* summ;      // [B*S]
-  const uint64_t* cand;   // [B*S*SEG]
+  const uint4* summ;        // [B*S]
+  const uint64_t* cand;     // [B*S*SEG]
   int S, SEG;
+  const uint32_t* rowflag;  // [B] history flags of K0
 };
 
 __global__ void __launch_bounds__(NT, 1) lss_resolve_kernel(const RowArgs a, const GatherArgs g) {
@@ -220,6 +221,7 @@ __global__ void __launch_bounds__(NT, 1) lss_resolve_kernel(const RowArgs a, con
   const bool tk_on = k > 0 && k < V;
   const bool mp_on = mp > 0.0f && mp < 1.0f;
   const bool bounded = greedy || tk_on || mp_on || V <= FAST_CAP / 2;
+  if (tid == 0 && g.rowflag[row]) atomicOr(a.err, g.rowflag[row]);
   if (greedy) {
     if (warp == 0) {
       uint64_t b = 0;

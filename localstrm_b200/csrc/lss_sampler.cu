@@ -1,10 +1,10 @@
 // lss_sampler.cu — batched token sampler for B200 (sm_100a): the one translation unit of
 // liblss.so.  It holds the C ABI of include/lsampler.h and the host-side launch logic; the
 // kernels live in the headers it includes:
+//   lss_prep.cuh   K0  history (id, count) pairs per slice; K3's per-row preparation
 //   lss_scan.cuh   K1  persistent streaming pass over the logits (the hot path)
 //   lss_resolve.cuh K2 per-row gather of K1's candidates, sort / top-k / top-p / draw
 //   lss_slow.cuh   K3  rows K2 defers (dense radix select, NaN guard)
-//   lss_prep.cuh       history (id, count) pairs per CTA slice for K3
 //   lss_common.cuh     keys, PTX wrappers, reductions
 // plus lss_argmax_kernel below (the all-greedy seam, llm_engine.py:1139-1141).
 // What is computed, per row (LocalStrm src/engine/sampling.py:118-163): greedy argmax of the
@@ -22,6 +22,7 @@
 
 #include "lsampler.h"
 #include "lss_common.cuh"
+#include "lss_prep.cuh"
 #include "lss_scan.cuh"
 #include "lss_resolve.cuh"
 #include "lss_slow.cuh"
@@ -132,11 +133,13 @@ static Plan make_plan(int V) {
 }
 
 // Workspace: header (word 0 error flags, word 2 deferred-row count), row path codes, the
-// scan kernel's item summaries and candidate segments, the deferred-row list, and for the
-// second kernel the per-slice segments of the unique history ids, the ids and counts, and
-// the global hash table for rows with long histories.  row_path sits at a fixed offset.
+// scan kernel's item summaries and candidate segments, the per-slice segments of the unique
+// history pairs (for the second kernel's slices and for the scan kernel's), per-row history
+// flags, the deferred-row list, the pair arrays and the global hash table for rows with long
+// histories.  row_path sits at a fixed offset.
 struct WsLayout {
-  size_t header, row_path, summ, cand, seg_off, defer_rows, uniq_ids, uniq_cnt, gkeys, gcnts, total;
+  size_t header, row_path, summ, cand, seg_off, seg2, rowflag, defer_rows, uniq_ids, uniq_cnt, gkeys, gcnts,
+      total;
 };
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 static WsLayout ws_layout(int B, int V, int64_t H) {
@@ -150,9 +153,11 @@ static WsLayout ws_layout(int B, int V, int64_t H) {
   L.summ = o; o = align256(o + 16 * items);
   L.cand = o; o = align256(o + 8 * items * (size_t)pl.SEG);
   L.seg_off = o; o = align256(o + 4 * b * (MAXCL + 1));
+  L.seg2 = o; o = align256(o + 4 * b * (size_t)(pl.S + 1));
+  L.rowflag = o; o = align256(o + 4 * b);
   L.defer_rows = o; o = align256(o + 4 * b);
-  L.uniq_ids = o; o = align256(o + 4 * h);
-  L.uniq_cnt = o; o = align256(o + 4 * h);
+  L.uniq_ids = o; o = align256(o + 4 * (h + 4));   // 4 entries of padding: 16-byte copy windows
+  L.uniq_cnt = o; o = align256(o + 4 * (h + 4));
   L.gkeys = o; o = align256(o + 8 * h);
   L.gcnts = o; o = align256(o + 8 * h);
   L.total = o;
@@ -369,8 +374,33 @@ int lss_sample_prepare(int B, int V, const float* temperature, const int32_t* to
     return LSS_ERR_INVALID_ARG;
   if (hist_total > 0 && !hist_ids) return LSS_ERR_INVALID_ARG;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // The header (error flags, deferred-row count) starts every call at zero.
-  if (cudaMemsetAsync(workspace, 0, 256, st) != cudaSuccess) return LSS_ERR_CUDA;
+  unsigned char* ws = reinterpret_cast<unsigned char*>(workspace);
+  const WsLayout L = ws_layout(B, V, hist_total);
+  const Plan pl = make_plan(V);
+  HistArgs h{};
+  h.r.B = B;
+  h.r.V = V;
+  h.r.use_hist = hist_total > 0 ? 1 : 0;
+  h.r.temperature = temperature;
+  h.r.top_k = top_k;
+  h.r.min_p = min_p;
+  h.r.rep = repetition_penalty;
+  h.r.freq = frequency_penalty;
+  h.r.pres = presence_penalty;
+  h.r.hist_off = hist_offsets;
+  h.r.hist_ids = hist_ids;
+  h.r.uniq_ids = reinterpret_cast<int32_t*>(ws + L.uniq_ids);
+  h.r.uniq_cnt = reinterpret_cast<int32_t*>(ws + L.uniq_cnt);
+  h.r.gkeys = reinterpret_cast<uint32_t*>(ws + L.gkeys);
+  h.r.gcnts = reinterpret_cast<uint32_t*>(ws + L.gcnts);
+  h.S = pl.S;
+  h.TS = pl.TS;
+  h.seg2 = reinterpret_cast<int32_t*>(ws + L.seg2);
+  h.rowflag = reinterpret_cast<uint32_t*>(ws + L.rowflag);
+  h.header = reinterpret_cast<uint32_t*>(ws + L.header);
+  // K0 also clears the header (error flags, deferred-row count) for this call.
+  lss_hist_kernel<<<B, HIST_NT, 0, st>>>(h);
+  if (cudaGetLastError() != cudaSuccess) return LSS_ERR_CUDA;
   return LSS_OK;
 }
 
@@ -406,7 +436,6 @@ int lss_sample_rows(const void* logits, int dtype, int B, int V, int64_t row_str
   sa.SEG = pl.SEG;
   sa.tile_bytes = pl.scan_tile;
   sa.use_hist = hist_total > 0 ? 1 : 0;
-  sa.hist_total = hist_total;
   sa.temperature = temperature;
   sa.top_k = top_k;
   sa.min_p = min_p;
@@ -414,7 +443,9 @@ int lss_sample_rows(const void* logits, int dtype, int B, int V, int64_t row_str
   sa.freq = frequency_penalty;
   sa.pres = presence_penalty;
   sa.hist_off = hist_offsets;
-  sa.hist_ids = hist_ids;
+  sa.uniq_ids = reinterpret_cast<const int32_t*>(ws + L.uniq_ids);
+  sa.uniq_cnt = reinterpret_cast<const int32_t*>(ws + L.uniq_cnt);
+  sa.seg2 = reinterpret_cast<const int32_t*>(ws + L.seg2);
   sa.summ = reinterpret_cast<uint4*>(ws + L.summ);
   sa.cand = reinterpret_cast<uint64_t*>(ws + L.cand);
   sa.err = header;
@@ -454,6 +485,7 @@ int lss_sample_rows(const void* logits, int dtype, int B, int V, int64_t row_str
   ga.cand = sa.cand;
   ga.S = pl.S;
   ga.SEG = pl.SEG;
+  ga.rowflag = reinterpret_cast<const uint32_t*>(ws + L.rowflag);
   cudaError_t e;
   switch (dtype) {
     case LSS_DTYPE_F32: e = launch_rows<LSS_DTYPE_F32>(sa, a, ga, pl, B, st); break;

@@ -7,12 +7,11 @@
 //
 //  * 1 producer warp: fetches each item's row parameters with cp.async several items ahead;
 //    when a stage of the two-stage ring is free it describes the item in shared memory and
-//    starts two bulk async copies into the stage — the slice of logits and the row's history
-//    ids — so the next slice streams in while the current one is processed.
-//  * 31 compute warps, per item: the history ids that fall in the slice are counted in
-//    16-bit shared counters, one per vocabulary entry of the slice (torch.unique of the
-//    history, sampling.py:52), and the penalties applied once per unique id
-//    (sampling.py:55-66); the slice max of the pre-temperature values z
+//    starts bulk async copies into the stage — the slice of logits and the slice's history
+//    pairs — so the next slice streams in while the current one is processed.
+//  * 31 compute warps, per item: the penalties (sampling.py:55-66) from the slice's unique
+//    (id, count) history pairs that K0 prepared (torch.unique, sampling.py:52); the slice
+//    max of the pre-temperature values z
 //    (held in registers, so each logit is read from shared memory once); the candidate
 //    threshold; the candidates written to the item's segment in global memory and a 16-byte
 //    summary (slice max or argmax code, candidate count, flags).
@@ -36,21 +35,20 @@ constexpr int SC_PROD = SC_CW;                // index of the producer warp
 constexpr int SC_R = 5;                       // float4 of the slice per compute thread
 constexpr int SC_TS_MAX = 19200;              // logits per slice (<= SC_CT * SC_R * 4)
 static_assert(SC_TS_MAX <= SC_CT * SC_R * 4, "a slice must fit the compute threads' registers");
-constexpr int SC_HB = 2048;                   // history ids staged per item
-constexpr int SC_HMAX = 65535;                // longest history counted in 16-bit counters
+constexpr int SC_HB = 2048;                   // words of history pairs staged per item
+constexpr int SC_HP = SC_HB / 2;              // (id, count) pairs staged per item
 constexpr int SC_RING = 8;                    // parameter ring (items)
 constexpr int SC_AHEAD = 4;                   // parameters fetched this many items ahead
 constexpr int SC_BAR = 3;                     // named barrier of the compute warps
 constexpr int SC_SEG_MIN = 256;               // candidate slots per item (at least)
 
 constexpr int ITEM_END = 0, ITEM_SKIP = 1, ITEM_GREEDY = 2, ITEM_SAMPLE = 3;
-// Summary flags: NaN / +inf in the slice or y overflow; top-k window deeper than the bins;
-// a history longer than the 16-bit counters.
-constexpr uint32_t SUM_SPECIAL = 1u, SUM_FAR = 2u, SUM_HASH = 4u;
+// Summary flags: NaN / +inf in the slice or y overflow; top-k window deeper than the bins.
+constexpr uint32_t SUM_SPECIAL = 1u, SUM_FAR = 2u;
 
 struct __align__(16) ItemDesc {
   int row, slice, mode, nb;     // nb: bytes of the slice the bulk copy stages
-  int hcount, hb, hlead, hbn;   // history: ids (0: no penalties), CSR base, staged window
+  int hcount, hb, hlead, hbn;   // history pairs of the slice, index of the first, staged window
   float T, rep, freq, pres;
   int k, lo, n, pad0;           // k: top-k when active (0 < k < V), else 0; slice [lo, lo + n)
   float tl;                     // min-p: T * ln(min_p) (0: inactive), the floor's offset in z
@@ -66,7 +64,7 @@ struct __align__(16) ScanCtl {
   ItemScratch sc[2];
   uint64_t best[2][32];         // greedy items: argmax code per warp
   uint32_t wkey[2][32];         // sampled items: max key of z per warp (all ones: NaN / +inf)
-  uint32_t prm[SC_RING][8];     // T, k, min_p, rep, freq, pres, hist_off[row], hist_off[row+1]
+  uint32_t prm[SC_RING][12];    // T, k, min_p, rep, freq, pres, hist_off[row], segment bounds
 };
 
 struct ScanArgs {
@@ -75,7 +73,6 @@ struct ScanArgs {
   int B, V, S, TS, SEG;
   int tile_bytes;               // tile part of a stage (multiple of 128 bytes)
   int use_hist;
-  int64_t hist_total;
   const float* temperature;
   const int32_t* top_k;
   const float* min_p;
@@ -83,7 +80,9 @@ struct ScanArgs {
   const float* freq;
   const float* pres;
   const int32_t* hist_off;
-  const int32_t* hist_ids;
+  const int32_t* uniq_ids;      // history pairs by slice (K0), with 4 entries of padding
+  const int32_t* uniq_cnt;      // either side
+  const int32_t* seg2;          // [B][S + 1] slice segments of the pairs
   uint4* summ;                  // [B*S]: {a lo, a hi, count, flags}
   uint64_t* cand;               // [B*S*SEG]: (key(z) << 32) | ~index
   uint32_t* err;
@@ -91,18 +90,8 @@ struct ScanArgs {
 
 __host__ __device__ constexpr int scan_stage_bytes(int tile_bytes) { return tile_bytes + SC_HB * 4; }
 __host__ __device__ constexpr int scan_smem_bytes(int tile_bytes) {
-  return 2 * scan_stage_bytes(tile_bytes) + SC_TS_MAX * 2 + (((NBIN + 1) * 4 + 15) & ~15) +
+  return 2 * scan_stage_bytes(tile_bytes) + (((NBIN + 1) * 4 + 15) & ~15) +
          (int)((sizeof(ScanCtl) + 15) & ~15);
-}
-
-// Penalties of one float4 of the slice from its four 16-bit history counts (zero: untouched).
-__device__ __noinline__ void apply4(float4* p, uint2 c, float rp, float fq, float pr) {
-  float4 x = *p;
-  if (c.x & 0xffffu) x.x = penalise(x.x, rp, fq, pr, (int)(c.x & 0xffffu));
-  if (c.x >> 16) x.y = penalise(x.y, rp, fq, pr, (int)(c.x >> 16));
-  if (c.y & 0xffffu) x.z = penalise(x.z, rp, fq, pr, (int)(c.y & 0xffffu));
-  if (c.y >> 16) x.w = penalise(x.w, rp, fq, pr, (int)(c.y >> 16));
-  *p = x;
 }
 
 __device__ __forceinline__ void sc_sync() { asm volatile("bar.sync %0, %1;" ::"n"(SC_BAR), "n"(SC_CT) : "memory"); }
@@ -113,16 +102,12 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int stage_bytes = scan_stage_bytes(a.tile_bytes);
-  // History counts of the slice: two 16-bit counters per word (entry i in word i / 2), zero
-  // between items (each compute thread resets the counters of its own entries).
-  uint32_t* hcnt2 = reinterpret_cast<uint32_t*>(smem + 2 * stage_bytes);
-  uint32_t* HL = hcnt2 + SC_TS_MAX / 2;
+  uint32_t* HL = reinterpret_cast<uint32_t*>(smem + 2 * stage_bytes);
   ScanCtl* ctl = reinterpret_cast<ScanCtl*>(reinterpret_cast<unsigned char*>(HL) + (((NBIN + 1) * 4 + 15) & ~15));
   const int V = a.V, S = a.S, TS = a.TS;
   const int nitems = a.B * S;
   const int G = gridDim.x;
 
-  for (int i = tid; i < SC_TS_MAX / 2; i += SC_NT) hcnt2[i] = 0u;
   if (tid < (int)(2 * sizeof(ItemScratch) / 4)) reinterpret_cast<uint32_t*>(ctl->sc)[tid] = 0u;  // cnt, flags
   if (tid == 0) {
     mbar_init(&ctl->full[0], 1);
@@ -137,10 +122,12 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
     // =====================================================================================
     // Producer warp
     // =====================================================================================
-    auto fetch = [&](int j) {  // parameters of item j into ring slot j % SC_RING (lanes 0..7)
+    auto fetch = [&](int j) {  // parameters of item j into ring slot j % SC_RING (lanes 0..8)
       const int t = blockIdx.x + j * G;
-      if (t < nitems && lane < 8) {
+      if (t < nitems && lane < 9) {
         const int row = t / S;
+        int slice = t - row * S + row;
+        slice -= (slice / S) * S;
         uint32_t* dst = &ctl->prm[j % SC_RING][lane];
         const void* src = nullptr;
         switch (lane) {
@@ -150,7 +137,8 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
           case 3: src = a.rep + row; break;
           case 4: src = a.freq + row; break;
           case 5: src = a.pres + row; break;
-          default: src = a.use_hist ? static_cast<const void*>(a.hist_off + row + (lane - 6)) : nullptr; break;
+          case 6: src = a.use_hist ? static_cast<const void*>(a.hist_off + row) : nullptr; break;
+          default: src = a.seg2 + (int64_t)row * (S + 1) + slice + (lane - 7); break;
         }
         if (src) cp_async4(dst, src);
         else *dst = 0u;
@@ -158,7 +146,6 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
       cp_async_commit();
     };
     for (int j = 0; j < SC_AHEAD; ++j) fetch(j);
-    const uintptr_t hbase = reinterpret_cast<uintptr_t>(a.hist_ids);
     for (int j = 0;; ++j) {
       const int s = j & 1;
       const int t = blockIdx.x + j * G;
@@ -170,7 +157,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
         // copies follow the wait.
         ItemDesc nd{};
         const char* g0 = nullptr;
-        uintptr_t w0 = 0;
+        uintptr_t w0 = 0;  // first staged pair (index into the pair arrays)
         nd.mode = ITEM_END;
         if (t < nitems) {
           const uint32_t* p = ctl->prm[j % SC_RING];
@@ -183,7 +170,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
           const int k = (int)p[1];
           const float mp = __uint_as_float(p[2]);
           const float rp = __uint_as_float(p[3]), fq = __uint_as_float(p[4]), pr = __uint_as_float(p[5]);
-          const int h0 = (int)p[6], h1 = (int)p[7];
+          const int hoff = (int)p[6], s0 = (int)p[7], s1 = (int)p[8];
           const bool greedy = T <= 0.0f;
           // Rows whose survivors are not bounded (top-p only or no filter on a large
           // vocabulary) go to the second kernel whole; their slices are not read here.
@@ -193,30 +180,21 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
           const int n = min(V, lo + TS) - lo;
           g0 = reinterpret_cast<const char*>(a.logits) + ((int64_t)row * a.row_stride + lo) * ES;
           const int nb = (mode != ITEM_SKIP && (reinterpret_cast<uintptr_t>(g0) & 15) == 0) ? ((n * ES) & ~15) : 0;
-          const int H = h1 - h0;
-          const bool pen = mode == ITEM_SAMPLE && a.use_hist && H > 0 && (rp != 1.0f || fq != 0.0f || pr != 0.0f);
-          // History window: the 16-byte blocks that cover ids [h0, h1), clipped to the
-          // 16-byte blocks inside the id array, at most SC_HB ids.
-          int hlead = 0, hbn = 0;
-          if (pen) {
-            const uintptr_t lo_ok = (hbase + 15) & ~(uintptr_t)15;
-            const uintptr_t hi_ok = (hbase + 4 * (uintptr_t)a.hist_total) & ~(uintptr_t)15;
-            const uintptr_t b0 = hbase + 4 * (uintptr_t)h0, b1 = hbase + 4 * (uintptr_t)h1;
-            w0 = b0 & ~(uintptr_t)15;
-            if (w0 < lo_ok) w0 = lo_ok;
-            uintptr_t w1 = (b1 + 15) & ~(uintptr_t)15;
-            if (w1 > hi_ok) w1 = hi_ok;
-            if (w1 > w0) {
-              hbn = (int)min((uintptr_t)(SC_HB * 4), w1 - w0) / 4;
-              hlead = (int)((intptr_t)b0 - (intptr_t)w0) / 4;
-            }
+          // History pairs of this slice (K0): the 16-byte blocks that cover them, at most SC_HP.
+          const int np = mode == ITEM_SAMPLE ? s1 - s0 : 0;
+          int hlead = 0, hbn = 0, hb = hoff + s0;
+          if (np > 0) {
+            const int w0i = hb & ~3;
+            hlead = hb - w0i;
+            hbn = min(((hb + np + 3) & ~3) - w0i, SC_HP);
+            w0 = (uintptr_t)w0i;
           }
           nd.row = row;
           nd.slice = slice;
           nd.mode = mode;
           nd.nb = nb;
-          nd.hcount = pen ? H : 0;
-          nd.hb = h0;
+          nd.hcount = np;
+          nd.hb = hb;
           nd.hlead = hlead;
           nd.hbn = hbn;
           nd.T = T;
@@ -233,13 +211,15 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
         if (j >= 2 && !mbar_wait_bounded_sleep(&ctl->empty[s], (uint32_t)(((j >> 1) - 1) & 1)))
           atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
         ctl->desc[s] = nd;
-        mbar_expect_tx(&ctl->full[s], (uint32_t)(nd.nb + nd.hbn * 4));
+        mbar_expect_tx(&ctl->full[s], (uint32_t)(nd.nb + nd.hbn * 8));
         unsigned char* dst = smem + s * stage_bytes;
         constexpr int CH = 32768;
         for (int off = 0; off < nd.nb; off += CH)
           bulk_g2s(dst + off, g0 + off, (uint32_t)min(CH, nd.nb - off), &ctl->full[s]);
-        if (nd.hbn > 0)
-          bulk_g2s(dst + a.tile_bytes, reinterpret_cast<const void*>(w0), (uint32_t)(nd.hbn * 4), &ctl->full[s]);
+        if (nd.hbn > 0) {
+          bulk_g2s(dst + a.tile_bytes, a.uniq_ids + w0, (uint32_t)(nd.hbn * 4), &ctl->full[s]);
+          bulk_g2s(dst + a.tile_bytes + SC_HP * 4, a.uniq_cnt + w0, (uint32_t)(nd.hbn * 4), &ctl->full[s]);
+        }
       }
       __syncwarp();
       if (t >= nitems) break;
@@ -328,28 +308,21 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
       tile[n + ctid] = -INFINITY;
       wrote = true;
     }
-    // ---- history ids in the slice counted (one shared add per occurrence, no return value)
-    const int H = D.hcount;
-    if (H > 0 && H <= SC_HMAX) {
-      const int32_t* hs = reinterpret_cast<const int32_t*>(smem + s * stage_bytes + a.tile_bytes);
+    // ---- history penalties (sampling.py:55-66), once per unique id of the slice
+    const int np = D.hcount;
+    // Entries written above by other threads (plain loads, widening) are complete first.
+    if (np > 0 && (nbulk < n || DT != LSS_DTYPE_F32)) sc_sync();
+    if (np > 0) {
+      const int32_t* ids = reinterpret_cast<const int32_t*>(smem + s * stage_bytes + a.tile_bytes);
+      const int32_t* cnt = ids + SC_HP;
       const int hlead = D.hlead, hbn = D.hbn, hb = D.hb;
-      constexpr int HU = 3;
-      for (int j0 = 0; j0 < H; j0 += SC_CT * HU) {
-        int idl[HU];
-#pragma unroll
-        for (int u = 0; u < HU; ++u) {
-          const int jj2 = j0 + u * SC_CT + ctid;
-          idl[u] = -1;
-          if (jj2 < H) {
-            const int w = jj2 + hlead;
-            const int raw = (w >= 0 && w < hbn) ? hs[w] : a.hist_ids[hb + jj2];
-            if ((unsigned)raw >= (unsigned)V) atomicOr(a.err, LSS_FLAG_BAD_HISTORY);
-            else if ((unsigned)(raw - lo) < (unsigned)n) idl[u] = raw - lo;
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < HU; ++u)
-          if (idl[u] >= 0) atomicAdd(&hcnt2[idl[u] >> 1], 1u << ((idl[u] & 1) << 4));
+      const float rp = D.rep, fq = D.freq, pr = D.pres;
+      for (int e = ctid; e < np; e += SC_CT) {
+        const int w = e + hlead;
+        const int id = w < hbn ? ids[w] : a.uniq_ids[hb + e];
+        const int c = w < hbn ? cnt[w] : a.uniq_cnt[hb + e];
+        tile[id - lo] = penalise(tile[id - lo], rp, fq, pr, c);
+        wrote = true;
       }
     }
     return true;
@@ -407,32 +380,15 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
       best = warp_allreduce(best, MaxU64());
       if (lane == 0) ctl->best[s][warp] = best;
     } else if (mode == ITEM_SAMPLE) {
-      // Penalties (sampling.py:55-66) once per unique id, from the counters of the thread's
-      // own entries, which it resets; then the slice max of z.
-      const int H = D.hcount;
-      const bool pen = H > 0 && H <= SC_HMAX;
-      float4* t4w = reinterpret_cast<float4*>(smem + s * stage_bytes);
+      // The slice max of z (penalties applied in the preparation).
 #pragma unroll
       for (int i = 0; i < SC_R; ++i) {
         const int q = i * SC_CT + ctid;
-        v[i] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-        if (q < n4) {
-          if (pen) {
-            uint2* cp = reinterpret_cast<uint2*>(hcnt2 + 2 * q);
-            const uint2 c = *cp;
-            if ((c.x | c.y) != 0u) {
-              apply4(t4w + q, c, D.rep, D.freq, D.pres);
-              *cp = make_uint2(0u, 0u);
-              wrote = true;
-            }
-          }
-          v[i] = t4[q];
-        }
+        v[i] = q < n4 ? t4[q] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
         tmax = fmax_nan(tmax, fmax_nan(fmax_nan(v[i].x, v[i].y), fmax_nan(v[i].z, v[i].w)));
       }
       const float wmax = warp_allreduce(tmax, MaxF());
       if (lane == 0) ctl->wkey[s][warp] = (!(wmax == wmax) || wmax == INFINITY) ? 0xffffffffu : f2key(wmax);
-      if (H > SC_HMAX && ctid == 0) atomicOr(&sc->flags, SUM_HASH);  // counts not kept
       if (k)
         for (int i = ctid; i < NBIN + 1; i += SC_CT) HL[i] = 0u;
     }

@@ -267,7 +267,11 @@ __device__ void slow_row(Row<CL>& R, const RowArgs& a, const int row, uint32_t& 
   // the segments to every CTA of the cluster.
   if (a.use_hist && R.me == 0) {
     uint32_t* hm = reinterpret_cast<uint32_t*>(tile);
-    prep_row(a, row, a.TE, CL, hm, hm + PREP_SMEM_SLOTS, hm + 2 * PREP_SMEM_SLOTS, hm + 2 * PREP_SMEM_SLOTS + 16);
+    const bool active = a.temperature[row] > 0.0f &&
+                        (a.rep[row] != 1.0f || a.freq[row] != 0.0f || a.pres[row] != 0.0f);
+    const PrepOut o{a.seg_off + (int64_t)row * (MAXCL + 1), a.err};
+    prep_row<NT>(a, row, active, a.TE, CL, o, hm, hm + PREP_SMEM_SLOTS, hm + 2 * PREP_SMEM_SLOTS,
+                 hm + 2 * PREP_SMEM_SLOTS + PREP_MAXSEG + 1, BlockSync());
   }
   // The previous row (or the history hash) wrote this tile through the generic proxy; order
   // that before the bulk copy of this row.
