@@ -2,7 +2,8 @@
 // (torch.unique of the history, sampling.py:52), grouped by vocabulary slice.
 //
 // prep_row does one row with the whole CTA: histories of up to PREP_SMEM_SLOTS / 2 ids hash
-// in the shared memory handed in, longer ones in a global table of 2H slots.  The pairs of
+// in the shared memory handed in (and the slots they occupy are listed, so that grouping
+// walks only those), longer ones in a global table of 2H slots.  The pairs of
 // slice c ([c*TE, (c+1)*TE)) land in uniq_ids / uniq_cnt[hist_off[row] + so[c] ..
 // hist_off[row] + so[c+1]).  K0, lss_hist_kernel, runs it for every row with the scan
 // kernel's slices; the second kernel runs it again for the rows it takes, with its own
@@ -22,12 +23,14 @@ struct PrepOut {
   uint32_t* bad;       // OR'ed with LSS_FLAG_BAD_HISTORY for an id outside [0, V)
 };
 
-// Whole CTA (NTH threads, `sync` its barrier).  `skeys` / `scnts`: PREP_SMEM_SLOTS words each;
-// `bcnt`: PREP_MAXSEG + 1 words, `bfill`: PREP_MAXSEG words.  `active`: the row's penalties
-// apply (otherwise only empty segments are written).
+// Whole CTA (NTH threads, `sync` its barrier).  Scratch `sw` in shared memory: PREP_SCRATCH_WORDS
+// words (hash keys and counts, the list of occupied slots, slice counters).  `active`: the
+// row's penalties apply (otherwise only empty segments are written).
+constexpr int PREP_SCRATCH_WORDS = 2 * PREP_SMEM_SLOTS + PREP_SMEM_SLOTS / 4 + 2 * (PREP_MAXSEG + 1) + 1;
+
 template <int NTH, class Sync>
-__device__ void prep_row(const RowArgs& a, int row, bool active, int TE, int nseg, const PrepOut& o,
-                         uint32_t* skeys, uint32_t* scnts, uint32_t* bcnt, uint32_t* bfill, Sync sync) {
+__device__ void prep_row(const RowArgs& a, int row, bool active, int TE, int nseg, const PrepOut& o, uint32_t* sw,
+                         Sync sync) {
   const int tid = threadIdx.x, lane = tid & 31;
   if (!active) {
     if (tid <= nseg) o.so[tid] = 0;
@@ -39,29 +42,37 @@ __device__ void prep_row(const RowArgs& a, int row, bool active, int TE, int nse
     if (tid <= nseg) o.so[tid] = 0;
     return;
   }
+  uint32_t* skeys = sw;
+  uint32_t* scnts = sw + PREP_SMEM_SLOTS;
+  uint16_t* slist = reinterpret_cast<uint16_t*>(sw + 2 * PREP_SMEM_SLOTS);  // PREP_SMEM_SLOTS / 2 entries
+  uint32_t* bcnt = sw + 2 * PREP_SMEM_SLOTS + PREP_SMEM_SLOTS / 4;
+  uint32_t* bfill = bcnt + PREP_MAXSEG + 1;
+  uint32_t* nlist = bfill + PREP_MAXSEG + 1;
   uint32_t *keys, *cnts;
   uint32_t cap;
-  bool pow2;
-  if (2 * H <= PREP_SMEM_SLOTS) {
+  const bool small = 2 * H <= PREP_SMEM_SLOTS;  // shared hash, occupied slots listed
+  if (small) {
     cap = (uint32_t)next_pow2(2 * H);
     keys = skeys;
     cnts = scnts;
-    pow2 = true;
   } else {
     cap = (uint32_t)(2 * H);
     keys = a.gkeys + 2 * (int64_t)b;
     cnts = a.gcnts + 2 * (int64_t)b;
-    pow2 = false;
   }
   for (uint32_t s = tid; s < cap; s += NTH) {
     keys[s] = EMPTY;
     cnts[s] = 0;
   }
-  if (tid <= PREP_MAXSEG) bcnt[tid] = 0;
-  if (tid < PREP_MAXSEG) bfill[tid] = 0;
+  if (tid <= PREP_MAXSEG) {
+    bcnt[tid] = 0;
+    bfill[tid] = 0;
+  }
+  if (tid == 0) *nlist = 0;
   sync();
   // Insert: lanes holding the same id are merged first (one atomic per distinct id per warp).
-  // U ids per thread are loaded before any is inserted, so their latencies overlap.
+  // U ids per thread are loaded before any is inserted, so their latencies overlap.  In the
+  // shared table a new key's slot is listed (one list reservation per warp).
   constexpr int U = 8;
   for (int j0 = 0; j0 < H; j0 += NTH * U) {
     int idv[U];
@@ -72,31 +83,49 @@ __device__ void prep_row(const RowArgs& a, int row, bool active, int TE, int nse
     }
 #pragma unroll
     for (int t = 0; t < U; ++t) {
+      if (j0 + t * NTH >= H) break;  // warp-uniform: no entry in this or later rounds
       int id = idv[t] == INT32_MIN ? -1 : idv[t];
       if (idv[t] != INT32_MIN && (id < 0 || id >= a.V)) {
         atomicOr(o.bad, LSS_FLAG_BAD_HISTORY);
         id = -1;
       }
       const unsigned same = __match_any_sync(0xffffffffu, id);
+      bool fresh = false;
+      uint32_t slot = 0;
       if (id >= 0 && lane == __ffs(same) - 1) {
         uint32_t h = (uint32_t)id * 2654435761u;
-        h = pow2 ? (h & (cap - 1)) : (h % cap);
+        h = small ? (h & (cap - 1)) : (h % cap);
         for (uint32_t probe = 0; probe < cap; ++probe) {
           const uint32_t old = atomicCAS(&keys[h], EMPTY, (uint32_t)id);
           if (old == EMPTY || old == (uint32_t)id) {
             atomicAdd(&cnts[h], (uint32_t)__popc(same));
+            fresh = old == EMPTY;
+            slot = h;
             break;
           }
           h = (h + 1 == cap) ? 0 : h + 1;
         }
       }
+      if (small) {
+        const uint32_t bal = __ballot_sync(0xffffffffu, fresh);
+        if (bal) {
+          const int leader = __ffs(bal) - 1;
+          uint32_t base = 0;
+          if (lane == leader) base = atomicAdd(nlist, (uint32_t)__popc(bal));
+          base = __shfl_sync(0xffffffffu, base, leader);
+          if (fresh) slist[base + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)slot;
+        }
+      }
     }
   }
   sync();
-  // Group by slice: count, exclusive scan, scatter (one atomic per slice per warp).
-  for (uint32_t s0 = 0; s0 < cap; s0 += NTH) {
-    const uint32_t s = s0 + tid;
-    const uint32_t k = s < cap ? keys[s] : EMPTY;
+  // Group by slice: count, exclusive scan, scatter (one atomic per slice per warp).  The
+  // shared table is walked through its list of occupied slots, the global one whole.
+  const uint32_t nwalk = small ? *nlist : cap;
+  for (uint32_t s0 = 0; s0 < nwalk; s0 += NTH) {
+    const uint32_t i = s0 + tid;
+    const uint32_t s = small ? (i < nwalk ? (uint32_t)slist[i] : 0u) : i;
+    const uint32_t k = i < nwalk ? keys[s] : EMPTY;
     const int c = k != EMPTY ? (int)(k / (uint32_t)TE) : -1;
     const unsigned same = __match_any_sync(0xffffffffu, c);
     if (c >= 0 && lane == __ffs(same) - 1) atomicAdd(&bcnt[c], (uint32_t)__popc(same));
@@ -111,9 +140,10 @@ __device__ void prep_row(const RowArgs& a, int row, bool active, int TE, int nse
     }
   }
   sync();
-  for (uint32_t s0 = 0; s0 < cap; s0 += NTH) {
-    const uint32_t s = s0 + tid;
-    const uint32_t k = s < cap ? keys[s] : EMPTY;
+  for (uint32_t s0 = 0; s0 < nwalk; s0 += NTH) {
+    const uint32_t i = s0 + tid;
+    const uint32_t s = small ? (i < nwalk ? (uint32_t)slist[i] : 0u) : i;
+    const uint32_t k = i < nwalk ? keys[s] : EMPTY;
     const int c = k != EMPTY ? (int)(k / (uint32_t)TE) : -1;
     const unsigned same = __match_any_sync(0xffffffffu, c);
     const int leader = __ffs(same) - 1;
@@ -137,8 +167,11 @@ struct BlockSync {
 // K0: history kernel — one CTA per row: the (id, count) pairs of the rows whose penalties
 // the scan kernel applies, grouped by its slices (seg2[row][0 .. S]); a per-row flag for ids
 // outside [0, V).  Block 0 clears the workspace status first (no other block writes it).
+// Histories of up to PREP_SMEM_SLOTS / 2 ids take a short path: the ids are requested before
+// the table is cleared, slice counts are taken as new keys enter, and one pass over the list
+// of occupied slots scatters the pairs; longer ones go through prep_row's global table.
 // =========================================================================================
-constexpr int HIST_NT = 512;
+constexpr int HIST_NT = 1024;
 
 struct HistArgs {
   RowArgs r;
@@ -149,23 +182,132 @@ struct HistArgs {
 };
 
 __global__ void __launch_bounds__(HIST_NT) lss_hist_kernel(const HistArgs h) {
-  __shared__ uint32_t skeys[PREP_SMEM_SLOTS];
-  __shared__ uint32_t scnts[PREP_SMEM_SLOTS];
-  __shared__ uint32_t bcnt[PREP_MAXSEG + 1];
-  __shared__ uint32_t bfill[PREP_MAXSEG];
+  __shared__ uint32_t sw[PREP_SCRATCH_WORDS];
   const RowArgs& a = h.r;
   const int row = blockIdx.x;
-  if (row == 0 && threadIdx.x < 64) h.header[threadIdx.x] = 0u;
-  if (threadIdx.x == 0) h.rowflag[row] = 0u;
+  const int tid = threadIdx.x, lane = tid & 31;
+  pdl_trigger();  // the scan kernel may launch and start its own set-up
+  if (row == 0 && tid < 64) h.header[tid] = 0u;
+  if (tid == 0) h.rowflag[row] = 0u;
   const float T = a.temperature[row];
   const int k = a.top_k[row];
   const float mp = a.min_p[row];
   const bool bounded = (k > 0 && k < a.V) || (mp > 0.0f && mp < 1.0f) || a.V <= FAST_CAP / 2;
   const bool active = a.use_hist && T > 0.0f && bounded &&
                       (a.rep[row] != 1.0f || a.freq[row] != 0.0f || a.pres[row] != 0.0f);
+  const int nseg = h.S;
+  int32_t* so = h.seg2 + (int64_t)row * (nseg + 1);
+  const PrepOut o{so, h.rowflag + row};
+  int H = 0, b = 0;
+  if (active) {
+    b = a.hist_off[row];
+    H = a.hist_off[row + 1] - b;
+  }
+  if (!active || H <= 0) {
+    if (tid <= nseg) so[tid] = 0;
+    return;
+  }
+  if (2 * H > PREP_SMEM_SLOTS) {
+    __syncthreads();  // rowflag cleared before prep_row may raise it
+    prep_row<HIST_NT>(a, row, true, h.TS, nseg, o, sw, BlockSync());
+    return;
+  }
+  // ---- short path: at most 2 ids per thread
+  constexpr int U = PREP_SMEM_SLOTS / 2 / HIST_NT;
+  int idv[U];
+#pragma unroll
+  for (int t = 0; t < U; ++t) {
+    const int j = t * HIST_NT + tid;
+    idv[t] = j < H ? a.hist_ids[b + j] : INT32_MIN;
+  }
+  uint32_t* keys = sw;
+  uint32_t* cnts = sw + PREP_SMEM_SLOTS;
+  uint16_t* slist = reinterpret_cast<uint16_t*>(sw + 2 * PREP_SMEM_SLOTS);
+  uint32_t* bcnt = sw + 2 * PREP_SMEM_SLOTS + PREP_SMEM_SLOTS / 4;
+  uint32_t* bfill = bcnt + PREP_MAXSEG + 1;
+  uint32_t* nlist = bfill + PREP_MAXSEG + 1;
+  const uint32_t cap = (uint32_t)next_pow2(2 * H);
+  for (uint32_t s2 = tid; s2 < cap; s2 += HIST_NT) {
+    keys[s2] = EMPTY;
+    cnts[s2] = 0;
+  }
+  if (tid <= PREP_MAXSEG) {
+    bcnt[tid] = 0;
+    bfill[tid] = 0;
+  }
+  if (tid == 0) *nlist = 0;
   __syncthreads();
-  const PrepOut o{h.seg2 + (int64_t)row * (h.S + 1), h.rowflag + row};
-  prep_row<HIST_NT>(a, row, active, h.TS, h.S, o, skeys, scnts, bcnt, bfill, BlockSync());
+  const uint32_t TS = (uint32_t)h.TS;
+#pragma unroll
+  for (int t = 0; t < U; ++t) {
+    if (t * HIST_NT >= H) break;  // warp-uniform
+    int id = idv[t] == INT32_MIN ? -1 : idv[t];
+    if (idv[t] != INT32_MIN && (id < 0 || id >= a.V)) {
+      atomicOr(o.bad, LSS_FLAG_BAD_HISTORY);
+      id = -1;
+    }
+    const unsigned same = __match_any_sync(0xffffffffu, id);
+    bool fresh = false;
+    uint32_t slot = 0;
+    if (id >= 0 && lane == __ffs(same) - 1) {
+      uint32_t hh = ((uint32_t)id * 2654435761u) & (cap - 1);
+      for (uint32_t probe = 0; probe < cap; ++probe) {
+        const uint32_t old = atomicCAS(&keys[hh], EMPTY, (uint32_t)id);
+        if (old == EMPTY || old == (uint32_t)id) {
+          atomicAdd(&cnts[hh], (uint32_t)__popc(same));
+          fresh = old == EMPTY;
+          slot = hh;
+          break;
+        }
+        hh = (hh + 1) & (cap - 1);
+      }
+    }
+    const uint32_t bal = __ballot_sync(0xffffffffu, fresh);
+    if (bal) {
+      const int leader = __ffs(bal) - 1;
+      uint32_t base = 0;
+      if (lane == leader) base = atomicAdd(nlist, (uint32_t)__popc(bal));
+      base = __shfl_sync(0xffffffffu, base, leader);
+      const int c = fresh ? (int)((uint32_t)id / TS) : -1;
+      const unsigned sc = __match_any_sync(0xffffffffu, c);
+      if (fresh) {
+        slist[base + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)slot;
+        if (lane == __ffs(sc) - 1) atomicAdd(&bcnt[c], (uint32_t)__popc(sc));
+      }
+    }
+  }
+  __syncthreads();
+  if (tid < 32) {
+    // Exclusive scan of the slice counts (lane c holds slice c; nseg <= 32).
+    const uint32_t v = lane < nseg ? bcnt[lane] : 0u;
+    uint32_t incl = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += y;
+    }
+    bcnt[lane] = incl - v;
+    if (lane <= nseg) so[lane] = (int32_t)(incl - v);
+    if (lane == 31 && nseg == 32) so[32] = (int32_t)incl;
+  }
+  __syncthreads();
+  const uint32_t L = *nlist;
+  for (uint32_t i0 = 0; i0 < L; i0 += HIST_NT) {  // warp-uniform trip count
+    const uint32_t i = i0 + tid;
+    const uint32_t s2 = i < L ? (uint32_t)slist[i] : 0u;
+    const uint32_t kk = i < L ? keys[s2] : EMPTY;
+    const int c = kk != EMPTY ? (int)(kk / TS) : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, c);
+    const int leader = __ffs(same) - 1;
+    uint32_t base = 0;
+    if (c >= 0 && lane == leader) base = atomicAdd(&bfill[c], (uint32_t)__popc(same));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (c >= 0) {
+      const uint32_t pos = bcnt[c] + base + (uint32_t)__popc(same & ((1u << lane) - 1u));
+      a.uniq_ids[b + pos] = (int32_t)kk;
+      a.uniq_cnt[b + pos] = (int32_t)cnts[s2];
+    }
+  }
 }
 
 }  // namespace lss

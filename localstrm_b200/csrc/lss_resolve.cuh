@@ -208,6 +208,7 @@ __global__ void __launch_bounds__(NT, 1) lss_resolve_kernel(const RowArgs a, con
   __shared__ uint32_t r32[NWARP];
   __shared__ int ri[NWARP];
   __shared__ uint32_t s_pre[33];
+  __shared__ uint32_t s_cnt[32];
   __shared__ uint32_t s_n, s_kmp;
   __shared__ int s_defer;
   __shared__ float s_my;
@@ -221,6 +222,8 @@ __global__ void __launch_bounds__(NT, 1) lss_resolve_kernel(const RowArgs a, con
   const bool tk_on = k > 0 && k < V;
   const bool mp_on = mp > 0.0f && mp < 1.0f;
   const bool bounded = greedy || tk_on || mp_on || V <= FAST_CAP / 2;
+  pdl_trigger();
+  pdl_wait();  // the scan kernel's summaries and candidates are complete and visible
   if (tid == 0 && g.rowflag[row]) atomicOr(a.err, g.rowflag[row]);
   if (greedy) {
     if (warp == 0) {
@@ -242,6 +245,12 @@ __global__ void __launch_bounds__(NT, 1) lss_resolve_kernel(const RowArgs a, con
     if (tid == 0) a.defer_rows[atomicAdd(&a.counters[2], 1u)] = row;
     return;
   }
+  // The first SPEC candidate slots of every slice are loaded with the summaries (their
+  // counts arrive with them), so that one dependent round trip is saved in the common case.
+  const int SPEC = min(16, NT / S);
+  uint64_t cspec = 0;
+  const int ss = tid / SPEC, si = tid - ss * SPEC;
+  if (ss < S) cspec = g.cand[((int64_t)row * S + ss) * g.SEG + si];
   if (warp == 0) {
     // Slice summaries (S <= 32): exact row max of z, flags, counts and their prefix.
     uint4 sm = make_uint4(0u, 0u, 0u, 0u);
@@ -249,14 +258,17 @@ __global__ void __launch_bounds__(NT, 1) lss_resolve_kernel(const RowArgs a, con
     const float mz = warp_allreduce(lane < S ? key2f(sm.x) : -INFINITY, MaxF());
     const uint32_t fl = warp_allreduce(sm.w, OrU32());
     const bool over = __ballot_sync(0xffffffffu, sm.z > (uint32_t)g.SEG) != 0u;
-    uint32_t incl = sm.z;
+    // Prefix of the counts beyond the speculated slots.
+    const uint32_t rest = sm.z > (uint32_t)SPEC ? sm.z - (uint32_t)SPEC : 0u;
+    uint32_t incl = rest;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += y;
     }
-    s_pre[lane] = incl - sm.z;
+    s_pre[lane] = incl - rest;
     if (lane == 31) s_pre[32] = incl;
+    s_cnt[lane] = sm.z;
     const float my = __fdiv_rn(mz, T);
     const bool special = !(my == my) || my == INFINITY || my == -INFINITY;
     if (lane == 0) {
@@ -273,17 +285,20 @@ __global__ void __launch_bounds__(NT, 1) lss_resolve_kernel(const RowArgs a, con
   }
   const float my = s_my;
   const uint32_t Kmp = s_kmp;
-  const uint32_t total = s_pre[32];
-  for (uint32_t i = tid; i < total; i += NT) {
-    int s = 0;
-    while (s + 1 < S && s_pre[s + 1] <= i) ++s;
-    const uint64_t c = g.cand[((int64_t)row * S + s) * g.SEG + (i - s_pre[s])];
+  auto consider = [&](uint64_t c) {
     const float y = __fdiv_rn(key2f((uint32_t)(c >> 32)), T);
     const uint32_t yk = f2key(y);
     if (y > -INFINITY && yk >= Kmp) {
       const uint32_t pos = atomicAdd(&s_n, 1u);
       if (pos < (uint32_t)FAST_CAP) G[pos] = ((uint64_t)yk << 32) | (uint32_t)c;
     }
+  };
+  if (ss < S && (uint32_t)si < s_cnt[ss]) consider(cspec);
+  const uint32_t total = s_pre[32];
+  for (uint32_t i = tid; i < total; i += NT) {
+    int sl = 0;
+    while (sl + 1 < S && s_pre[sl + 1] <= i) ++sl;
+    consider(g.cand[((int64_t)row * S + sl) * g.SEG + SPEC + (i - s_pre[sl])]);
   }
   __syncthreads();
   const uint32_t nk = s_n;

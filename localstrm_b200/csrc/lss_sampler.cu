@@ -118,7 +118,11 @@ static int slow_extra(int CL) {
 
 static Plan make_plan(int V) {
   Plan pl{};
-  pl.S = (V + SC_TS_MAX - 1) / SC_TS_MAX;
+  // Slices as large as the compute threads' registers and the copy ring allow.
+  const int fixed = scan_smem_bytes(0) - SC_NST * scan_stage_bytes(0);
+  const int tile_cap = ((SC_SMEM_MAX - fixed) / SC_NST - SC_HB * 4) / 128 * 128;
+  const int ts_max = std::min(SC_TS_MAX, tile_cap / 4 / 16 * 16);
+  pl.S = (V + ts_max - 1) / ts_max;
   pl.TS = round_up((V + pl.S - 1) / pl.S, 16);
   pl.SEG = std::max(SC_SEG_MIN, FAST_CAP / pl.S);
   pl.scan_tile = round_up(pl.TS * 4, 128);
@@ -229,21 +233,36 @@ static cudaError_t prepare_scan_kernel(K kern, KernelCfg& kc, int smem, int& nct
   return cudaSuccess;
 }
 
+// Launch with programmatic stream serialization (the kernel may start while the previous
+// kernel of the stream runs; it waits for it with griddepcontrol.wait), optionally clustered.
+template <class... KArgs, class... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem, int cluster,
+                              cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(block, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  int na = 0;
+  at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[na].val.programmaticStreamSerializationAllowed = 1;
+  ++na;
+  if (cluster > 1) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = (unsigned)cluster;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = (unsigned)na;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 template <class K>
 static cudaError_t launch_clusters(K kern, const RowArgs& a, int CL, int nclusters, int smem, cudaStream_t st) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3((unsigned)(nclusters * CL), 1, 1);
-  cfg.blockDim = dim3(NT, 1, 1);
-  cfg.dynamicSmemBytes = (size_t)smem;
-  cfg.stream = st;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = CL;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, a);
+  return launch_pdl(kern, (unsigned)(nclusters * CL), (unsigned)NT, (size_t)smem, CL, st, a);
 }
 
 // K1 (scan), K2 (resolve, one CTA per row), K3 (second kernel over the deferred list).
@@ -255,11 +274,10 @@ static cudaError_t launch_rows(const ScanArgs& sa, const RowArgs& ra, const Gath
   cudaError_t e = prepare_scan_kernel(lss_scan_kernel<DT>, scan_cfg, pl.scan_smem, nctas);
   if (e != cudaSuccess) return e;
   const int nitems = B * pl.S;
-  lss_scan_kernel<DT><<<std::min(nctas, nitems), SC_NT, pl.scan_smem, st>>>(sa);
-  e = cudaGetLastError();
+  e = launch_pdl(lss_scan_kernel<DT>, (unsigned)std::min(nctas, nitems), (unsigned)SC_NT, (size_t)pl.scan_smem, 1,
+                 st, sa);
   if (e != cudaSuccess) return e;
-  lss_resolve_kernel<<<B, NT, 0, st>>>(ra, ga);
-  e = cudaGetLastError();
+  e = launch_pdl(lss_resolve_kernel, (unsigned)B, (unsigned)NT, (size_t)0, 1, st, ra, ga);
   if (e != cudaSuccess) return e;
   int ncs = 0;
   switch (pl.CL) {

@@ -35,8 +35,10 @@ constexpr int SC_PROD = SC_CW;                // index of the producer warp
 constexpr int SC_R = 5;                       // float4 of the slice per compute thread
 constexpr int SC_TS_MAX = 19200;              // logits per slice (<= SC_CT * SC_R * 4)
 static_assert(SC_TS_MAX <= SC_CT * SC_R * 4, "a slice must fit the compute threads' registers");
+constexpr int SC_NST = 2;                     // stages of the copy ring
 constexpr int SC_HB = 2048;                   // words of history pairs staged per item
 constexpr int SC_HP = SC_HB / 2;              // (id, count) pairs staged per item
+constexpr int SC_SMEM_MAX = 232448;           // dynamic shared memory of one CTA
 constexpr int SC_RING = 8;                    // parameter ring (items)
 constexpr int SC_AHEAD = 4;                   // parameters fetched this many items ahead
 constexpr int SC_BAR = 3;                     // named barrier of the compute warps
@@ -58,10 +60,10 @@ struct __align__(16) ItemScratch {
   uint32_t cnt, flags, pad0, pad1;  // candidates, summary flags
 };
 struct __align__(16) ScanCtl {
-  uint64_t full[2];             // stage landed (1 arrival + bytes)
-  uint64_t empty[2];            // stage released (one arrival per compute warp)
-  ItemDesc desc[2];
-  ItemScratch sc[2];
+  uint64_t full[SC_NST];        // stage landed (1 arrival + bytes)
+  uint64_t empty[SC_NST];       // stage released (one arrival per compute warp)
+  ItemDesc desc[SC_NST];
+  ItemScratch sc[2];            // by item parity
   uint64_t best[2][32];         // greedy items: argmax code per warp
   uint32_t wkey[2][32];         // sampled items: max key of z per warp (all ones: NaN / +inf)
   uint32_t prm[SC_RING][12];    // T, k, min_p, rep, freq, pres, hist_off[row], segment bounds
@@ -90,7 +92,7 @@ struct ScanArgs {
 
 __host__ __device__ constexpr int scan_stage_bytes(int tile_bytes) { return tile_bytes + SC_HB * 4; }
 __host__ __device__ constexpr int scan_smem_bytes(int tile_bytes) {
-  return 2 * scan_stage_bytes(tile_bytes) + (((NBIN + 1) * 4 + 15) & ~15) +
+  return SC_NST * scan_stage_bytes(tile_bytes) + (((NBIN + 1) * 4 + 15) & ~15) +
          (int)((sizeof(ScanCtl) + 15) & ~15);
 }
 
@@ -102,7 +104,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int stage_bytes = scan_stage_bytes(a.tile_bytes);
-  uint32_t* HL = reinterpret_cast<uint32_t*>(smem + 2 * stage_bytes);
+  uint32_t* HL = reinterpret_cast<uint32_t*>(smem + SC_NST * stage_bytes);
   ScanCtl* ctl = reinterpret_cast<ScanCtl*>(reinterpret_cast<unsigned char*>(HL) + (((NBIN + 1) * 4 + 15) & ~15));
   const int V = a.V, S = a.S, TS = a.TS;
   const int nitems = a.B * S;
@@ -110,14 +112,15 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
 
   if (tid < (int)(2 * sizeof(ItemScratch) / 4)) reinterpret_cast<uint32_t*>(ctl->sc)[tid] = 0u;  // cnt, flags
   if (tid == 0) {
-    mbar_init(&ctl->full[0], 1);
-    mbar_init(&ctl->full[1], 1);
-    mbar_init(&ctl->empty[0], SC_CW);
-    mbar_init(&ctl->empty[1], SC_CW);
+    for (int q = 0; q < SC_NST; ++q) {
+      mbar_init(&ctl->full[q], 1);
+      mbar_init(&ctl->empty[q], SC_CW);
+    }
     fence_barrier_init();
   }
   __syncthreads();
 
+  pdl_trigger();  // the resolve kernel may launch; it waits for this grid before reading
   if (warp == SC_PROD) {
     // =====================================================================================
     // Producer warp
@@ -145,9 +148,10 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
       }
       cp_async_commit();
     };
+    pdl_wait();  // K0's pairs and segments are complete and visible
     for (int j = 0; j < SC_AHEAD; ++j) fetch(j);
     for (int j = 0;; ++j) {
-      const int s = j & 1;
+      const int s = j % SC_NST;
       const int t = blockIdx.x + j * G;
       cp_async_wait_group<SC_AHEAD - 1>();  // item j's parameters have landed
       __syncwarp();
@@ -208,7 +212,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
           nd.sb = __fdiv_rn(BIN_PER_NAT, T);
           nd.binw = __fdiv_rn(T, BIN_PER_NAT);
         }
-        if (j >= 2 && !mbar_wait_bounded_sleep(&ctl->empty[s], (uint32_t)(((j >> 1) - 1) & 1)))
+        if (j >= SC_NST && !mbar_wait_bounded(&ctl->empty[s], (uint32_t)((j / SC_NST - 1) & 1)))
           atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
         ctl->desc[s] = nd;
         mbar_expect_tx(&ctl->full[s], (uint32_t)(nd.nb + nd.hbn * 8));
@@ -245,8 +249,8 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
   bool wrote = false;  // this thread wrote the stage through the generic proxy
   // Waits for item jj's stage and prepares it; false at the end of the list (uniform).
   auto prepare = [&](int jj) -> bool {
-    const int s = jj & 1;
-    if (!mbar_wait_bounded_sleep(&ctl->full[s], (uint32_t)((jj >> 1) & 1)) && ctid == 0)
+    const int s = jj % SC_NST;
+    if (!mbar_wait_bounded_sleep(&ctl->full[s], (uint32_t)((jj / SC_NST) & 1)) && ctid == 0)
       atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
     const ItemDesc& D = ctl->desc[s];
     const int mode = D.mode;
@@ -347,10 +351,11 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
     }
   };
 
+  pdl_wait();
   if (!prepare(0)) return;
   for (int j = 0;; ++j) {
-    const int s = j & 1;
-    ItemScratch* sc = &ctl->sc[s];
+    const int s = j % SC_NST, ip = j & 1;  // stage, item parity (scratch)
+    ItemScratch* sc = &ctl->sc[ip];
     const ItemDesc& D = ctl->desc[s];
     sc_sync();  // item j: slice and history counts complete; item j-1 done by every warp
     if (warp == 0) write_summary();
@@ -378,7 +383,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
         }
       }
       best = warp_allreduce(best, MaxU64());
-      if (lane == 0) ctl->best[s][warp] = best;
+      if (lane == 0) ctl->best[ip][warp] = best;
     } else if (mode == ITEM_SAMPLE) {
       // The slice max of z (penalties applied in the preparation).
 #pragma unroll
@@ -388,7 +393,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
         tmax = fmax_nan(tmax, fmax_nan(fmax_nan(v[i].x, v[i].y), fmax_nan(v[i].z, v[i].w)));
       }
       const float wmax = warp_allreduce(tmax, MaxF());
-      if (lane == 0) ctl->wkey[s][warp] = (!(wmax == wmax) || wmax == INFINITY) ? 0xffffffffu : f2key(wmax);
+      if (lane == 0) ctl->wkey[ip][warp] = (!(wmax == wmax) || wmax == INFINITY) ? 0xffffffffu : f2key(wmax);
       if (k)
         for (int i = ctid; i < NBIN + 1; i += SC_CT) HL[i] = 0u;
     }
@@ -404,7 +409,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
     // ---- X(j)
     uint32_t mk = 0;
     if (mode == ITEM_SAMPLE) {
-      mk = lane < SC_CW ? ctl->wkey[s][lane] : 0u;
+      mk = lane < SC_CW ? ctl->wkey[ip][lane] : 0u;
       mk = warp_allreduce(mk, MaxU32());
       const bool special = mk == 0xffffffffu;
       if (special && ctid == 0) atomicOr(&sc->flags, SUM_SPECIAL);
@@ -508,7 +513,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
     pmode = mode;
     prow = row;
     pslice = slice;
-    ps = s;
+    ps = ip;
     pkey = mk;
     if (!prepare(j + 1)) break;
   }

@@ -270,8 +270,7 @@ __device__ void slow_row(Row<CL>& R, const RowArgs& a, const int row, uint32_t& 
     const bool active = a.temperature[row] > 0.0f &&
                         (a.rep[row] != 1.0f || a.freq[row] != 0.0f || a.pres[row] != 0.0f);
     const PrepOut o{a.seg_off + (int64_t)row * (MAXCL + 1), a.err};
-    prep_row<NT>(a, row, active, a.TE, CL, o, hm, hm + PREP_SMEM_SLOTS, hm + 2 * PREP_SMEM_SLOTS,
-                 hm + 2 * PREP_SMEM_SLOTS + PREP_MAXSEG + 1, BlockSync());
+    prep_row<NT>(a, row, active, a.TE, CL, o, hm, BlockSync());
   }
   // The previous row (or the history hash) wrote this tile through the generic proxy; order
   // that before the bulk copy of this row.
@@ -658,6 +657,10 @@ __device__ void slow_row(Row<CL>& R, const RowArgs& a, const int row, uint32_t& 
 template <int CL, int DT>
 __global__ void __launch_bounds__(NT, 2) lss_slow_kernel(const RowArgs a) {
   extern __shared__ __align__(1024) unsigned char smem[];
+  pdl_wait();  // the resolve kernel's deferred list is complete and visible
+  const int ndefer = (int)a.counters[2];
+  const int NC = gridDim.x / CL, cid = blockIdx.x / CL;
+  if (cid >= ndefer) return;  // the same for every CTA of the cluster
   using SM = SlowLayout<CL>;
   Row<CL> R;
   R.me = (int)R.cl.block_rank();
@@ -687,8 +690,6 @@ __global__ void __launch_bounds__(NT, 2) lss_slow_kernel(const RowArgs a) {
     fence_barrier_init();
   }
   __syncthreads();
-  const int ndefer = (int)a.counters[2];
-  const int NC = gridDim.x / CL, cid = blockIdx.x / CL;
   uint32_t phase = 0;
   for (int i = cid; i < ndefer; i += NC) {
     R.row = a.defer_rows[i];
