@@ -116,6 +116,18 @@ int lss_sample_rows(const void* logits, int dtype, int B, int V, int64_t row_str
                     const float* uniforms, int32_t* tokens_out, uint8_t* kept_out,
                     float* probs_out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Profiling entry point: only the streaming pass of lss_sample_rows (K1: penalties, slice
+ * maxima and candidates into the workspace), without the per-row resolve.  It leaves no
+ * tokens; it exists so that the pass can be timed on its own.  Arguments as lss_sample_rows.
+ * No counterpart in the reference. */
+int lss_scan_pass(const void* logits, int dtype, int B, int V, int64_t row_stride,
+                  const float* temperature, const int32_t* top_k, const float* top_p,
+                  const float* min_p, const float* repetition_penalty,
+                  const float* frequency_penalty, const float* presence_penalty,
+                  const int32_t* hist_offsets, const int32_t* hist_ids, int64_t hist_total,
+                  const float* uniforms, int32_t* tokens_out, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
 /* Batched greedy argmax (NaN counts as largest, lowest index wins ties), the
  * all-greedy seam of the engine (llm_engine.py:1139-1141; torch.argmax semantics). */
 int lss_argmax(const void* logits, int dtype, int B, int V, int64_t row_stride,

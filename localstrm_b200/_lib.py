@@ -44,6 +44,9 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.lss_sample_rows.restype = c_int
     lib.lss_sample_rows.argtypes = [P, c_int, c_int, c_int, c_int64, P, P, P, P, P, P, P, P, P, c_int64,
                                     P, P, P, P, P, c_size_t, P]
+    lib.lss_scan_pass.restype = c_int
+    lib.lss_scan_pass.argtypes = [P, c_int, c_int, c_int, c_int64, P, P, P, P, P, P, P, P, P, c_int64,
+                                  P, P, P, c_size_t, P]
     lib.lss_sample_noalloc.restype = c_int
     lib.lss_sample_noalloc.argtypes = [P, c_int, c_int, c_int, c_int64, P, P, P, P, P, P, P, P, P,
                                        c_int64, P, P, P, P, P]

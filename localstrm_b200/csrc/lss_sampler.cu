@@ -268,7 +268,7 @@ static cudaError_t launch_clusters(K kern, const RowArgs& a, int CL, int ncluste
 // K1 (scan), K2 (resolve, one CTA per row), K3 (second kernel over the deferred list).
 template <int DT>
 static cudaError_t launch_rows(const ScanArgs& sa, const RowArgs& ra, const GatherArgs& ga, const Plan& pl, int B,
-                               cudaStream_t st) {
+                               cudaStream_t st, bool scan_only) {
   static KernelCfg scan_cfg{};
   int nctas = 0;
   cudaError_t e = prepare_scan_kernel(lss_scan_kernel<DT>, scan_cfg, pl.scan_smem, nctas);
@@ -276,7 +276,7 @@ static cudaError_t launch_rows(const ScanArgs& sa, const RowArgs& ra, const Gath
   const int nitems = B * pl.S;
   e = launch_pdl(lss_scan_kernel<DT>, (unsigned)std::min(nctas, nitems), (unsigned)SC_NT, (size_t)pl.scan_smem, 1,
                  st, sa);
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess || scan_only) return e;
   e = launch_pdl(lss_resolve_kernel, (unsigned)B, (unsigned)NT, (size_t)0, 1, st, ra, ga);
   if (e != cudaSuccess) return e;
   int ncs = 0;
@@ -422,12 +422,12 @@ int lss_sample_prepare(int B, int V, const float* temperature, const int32_t* to
   return LSS_OK;
 }
 
-int lss_sample_rows(const void* logits, int dtype, int B, int V, int64_t row_stride,
-                    const float* temperature, const int32_t* top_k, const float* top_p,
-                    const float* min_p, const float* repetition_penalty, const float* frequency_penalty,
-                    const float* presence_penalty, const int32_t* hist_offsets, const int32_t* hist_ids,
-                    int64_t hist_total, const float* uniforms, int32_t* tokens_out, uint8_t* kept_out,
-                    float* probs_out, void* workspace, size_t workspace_bytes, void* stream) {
+static int sample_rows(const void* logits, int dtype, int B, int V, int64_t row_stride, const float* temperature,
+                       const int32_t* top_k, const float* top_p, const float* min_p,
+                       const float* repetition_penalty, const float* frequency_penalty,
+                       const float* presence_penalty, const int32_t* hist_offsets, const int32_t* hist_ids,
+                       int64_t hist_total, const float* uniforms, int32_t* tokens_out, uint8_t* kept_out,
+                       float* probs_out, void* workspace, size_t workspace_bytes, void* stream, bool scan_only) {
   if (row_stride < V) return LSS_ERR_INVALID_ARG;
   if (dtype != LSS_DTYPE_F32 && dtype != LSS_DTYPE_BF16 && dtype != LSS_DTYPE_F16) return LSS_ERR_INVALID_ARG;
   int rc = check_common(B, V, hist_total, hist_offsets, workspace, workspace_bytes);
@@ -506,15 +506,36 @@ int lss_sample_rows(const void* logits, int dtype, int B, int V, int64_t row_str
   ga.rowflag = reinterpret_cast<const uint32_t*>(ws + L.rowflag);
   cudaError_t e;
   switch (dtype) {
-    case LSS_DTYPE_F32: e = launch_rows<LSS_DTYPE_F32>(sa, a, ga, pl, B, st); break;
-    case LSS_DTYPE_BF16: e = launch_rows<LSS_DTYPE_BF16>(sa, a, ga, pl, B, st); break;
-    default: e = launch_rows<LSS_DTYPE_F16>(sa, a, ga, pl, B, st); break;
+    case LSS_DTYPE_F32: e = launch_rows<LSS_DTYPE_F32>(sa, a, ga, pl, B, st, scan_only); break;
+    case LSS_DTYPE_BF16: e = launch_rows<LSS_DTYPE_BF16>(sa, a, ga, pl, B, st, scan_only); break;
+    default: e = launch_rows<LSS_DTYPE_F16>(sa, a, ga, pl, B, st, scan_only); break;
   }
   if (e != cudaSuccess) {
     cudaGetLastError();
     return LSS_ERR_CUDA;
   }
   return LSS_OK;
+}
+
+int lss_sample_rows(const void* logits, int dtype, int B, int V, int64_t row_stride,
+                    const float* temperature, const int32_t* top_k, const float* top_p,
+                    const float* min_p, const float* repetition_penalty, const float* frequency_penalty,
+                    const float* presence_penalty, const int32_t* hist_offsets, const int32_t* hist_ids,
+                    int64_t hist_total, const float* uniforms, int32_t* tokens_out, uint8_t* kept_out,
+                    float* probs_out, void* workspace, size_t workspace_bytes, void* stream) {
+  return sample_rows(logits, dtype, B, V, row_stride, temperature, top_k, top_p, min_p, repetition_penalty,
+                     frequency_penalty, presence_penalty, hist_offsets, hist_ids, hist_total, uniforms, tokens_out,
+                     kept_out, probs_out, workspace, workspace_bytes, stream, false);
+}
+
+int lss_scan_pass(const void* logits, int dtype, int B, int V, int64_t row_stride, const float* temperature,
+                  const int32_t* top_k, const float* top_p, const float* min_p, const float* repetition_penalty,
+                  const float* frequency_penalty, const float* presence_penalty, const int32_t* hist_offsets,
+                  const int32_t* hist_ids, int64_t hist_total, const float* uniforms, int32_t* tokens_out,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+  return sample_rows(logits, dtype, B, V, row_stride, temperature, top_k, top_p, min_p, repetition_penalty,
+                     frequency_penalty, presence_penalty, hist_offsets, hist_ids, hist_total, uniforms, tokens_out,
+                     nullptr, nullptr, workspace, workspace_bytes, stream, true);
 }
 
 int lss_sample(const void* logits, int dtype, int B, int V, int64_t row_stride, const float* temperature,
