@@ -128,6 +128,28 @@ int lss_scan_pass(const void* logits, int dtype, int B, int V, int64_t row_strid
                   const float* uniforms, int32_t* tokens_out, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/* Vocabulary-sharded sampling: each GPU holds columns [vocab_offset, vocab_offset + Vs) of
+ * every row (the reference runs one device per row; this is a mode of its own).  Step 1,
+ * lss_shard_topk, writes one record per row of the shard: the shard's K largest values of
+ * y = z / T as codes (key(y) << 32 | ~global index, value descending, index ascending), then
+ * the shard's max of y, the sum of exp(y - max), flags and the number of codes.  The caller
+ * gathers the records of all shards shard-major ([nshards][B] records, e.g. one NCCL
+ * all-gather) and runs step 2, lss_shard_merge: the reference's top-k with k = K (ties
+ * kept), top-p, renormalisation and the inverse-CDF draw over the union of the shards'
+ * candidates, which holds the row's K largest.  Penalties and min-p are not applied in this
+ * mode.  records_out must be 16-byte aligned; the merge workspace holds the status word
+ * (lss_read_status) and the row paths (lss_read_row_paths). */
+#define LSS_SHARD_MAX_K 256
+size_t lss_shard_record_bytes(int K);
+size_t lss_shard_merge_workspace_bytes(int B);
+int lss_shard_topk(const void* logits, int dtype, int B, int Vs, int64_t row_stride,
+                   int64_t vocab_offset, const float* temperature, int K, void* records_out,
+                   void* stream);
+int lss_shard_merge(const void* records, int nshards, int B, int K, int V_total,
+                    const float* temperature, const float* top_p, const float* uniforms,
+                    int32_t* tokens_out, uint8_t* kept_out, float* probs_out, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
 /* Batched greedy argmax (NaN counts as largest, lowest index wins ties), the
  * all-greedy seam of the engine (llm_engine.py:1139-1141; torch.argmax semantics). */
 int lss_argmax(const void* logits, int dtype, int B, int V, int64_t row_stride,

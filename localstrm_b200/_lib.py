@@ -47,6 +47,14 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.lss_scan_pass.restype = c_int
     lib.lss_scan_pass.argtypes = [P, c_int, c_int, c_int, c_int64, P, P, P, P, P, P, P, P, P, c_int64,
                                   P, P, P, c_size_t, P]
+    lib.lss_shard_record_bytes.restype = c_size_t
+    lib.lss_shard_record_bytes.argtypes = [c_int]
+    lib.lss_shard_merge_workspace_bytes.restype = c_size_t
+    lib.lss_shard_merge_workspace_bytes.argtypes = [c_int]
+    lib.lss_shard_topk.restype = c_int
+    lib.lss_shard_topk.argtypes = [P, c_int, c_int, c_int, c_int64, c_int64, P, c_int, P, P]
+    lib.lss_shard_merge.restype = c_int
+    lib.lss_shard_merge.argtypes = [P, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, c_size_t, P]
     lib.lss_sample_noalloc.restype = c_int
     lib.lss_sample_noalloc.argtypes = [P, c_int, c_int, c_int, c_int64, P, P, P, P, P, P, P, P, P,
                                        c_int64, P, P, P, P, P]

@@ -5,6 +5,7 @@
 //   lss_scan.cuh   K1  persistent streaming pass over the logits (the hot path)
 //   lss_resolve.cuh K2 per-row gather of K1's candidates, sort / top-k / top-p / draw
 //   lss_slow.cuh   K3  rows K2 defers (dense radix select, NaN guard)
+//   lss_shard.cuh      vocabulary-sharded mode: per-shard top-K records, merge and draw
 //   lss_common.cuh     keys, PTX wrappers, reductions
 // plus lss_argmax_kernel below (the all-greedy seam, llm_engine.py:1139-1141).
 // What is computed, per row (LocalStrm src/engine/sampling.py:118-163): greedy argmax of the
@@ -26,6 +27,7 @@
 #include "lss_scan.cuh"
 #include "lss_resolve.cuh"
 #include "lss_slow.cuh"
+#include "lss_shard.cuh"
 
 namespace lss {
 
@@ -611,6 +613,72 @@ int lss_sample_noalloc(const void* logits, int dtype, int B, int V, int64_t row_
   return lss_sample(logits, dtype, B, V, row_stride, temperature, top_k, top_p, min_p, repetition_penalty,
                     frequency_penalty, presence_penalty, hist_offsets, hist_ids, hist_total, uniforms,
                     tokens_out, kept_out, probs_out, ws, (size_t)LSS_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+size_t lss_shard_record_bytes(int K) { return K < 1 ? 0 : shard_record_bytes(K); }
+
+size_t lss_shard_merge_workspace_bytes(int B) {
+  if (B < 0) return 0;
+  return 256 + (((size_t)(B > 0 ? B : 1) * 4 + 255) & ~(size_t)255);
+}
+
+int lss_shard_topk(const void* logits, int dtype, int B, int Vs, int64_t row_stride, int64_t vocab_offset,
+                   const float* temperature, int K, void* records_out, void* stream) {
+  if (B < 0 || Vs < 1 || row_stride < Vs || vocab_offset < 0 || K < 1 || K > LSS_SHARD_MAX_K)
+    return LSS_ERR_INVALID_ARG;
+  if (vocab_offset + Vs > 0x7fffffffLL) return LSS_ERR_UNSUPPORTED;
+  if (dtype != LSS_DTYPE_F32 && dtype != LSS_DTYPE_BF16 && dtype != LSS_DTYPE_F16) return LSS_ERR_INVALID_ARG;
+  if (B == 0) return LSS_OK;
+  if (!logits || !temperature || !records_out || (reinterpret_cast<uintptr_t>(records_out) & 15) != 0)
+    return LSS_ERR_INVALID_ARG;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  unsigned char* rec = reinterpret_cast<unsigned char*>(records_out);
+  switch (dtype) {
+    case LSS_DTYPE_F32:
+      lss_shard_kernel<LSS_DTYPE_F32><<<B, NT, 0, st>>>(logits, row_stride, Vs, vocab_offset, temperature, K, rec);
+      break;
+    case LSS_DTYPE_BF16:
+      lss_shard_kernel<LSS_DTYPE_BF16><<<B, NT, 0, st>>>(logits, row_stride, Vs, vocab_offset, temperature, K, rec);
+      break;
+    default:
+      lss_shard_kernel<LSS_DTYPE_F16><<<B, NT, 0, st>>>(logits, row_stride, Vs, vocab_offset, temperature, K, rec);
+      break;
+  }
+  if (cudaGetLastError() != cudaSuccess) return LSS_ERR_CUDA;
+  return LSS_OK;
+}
+
+int lss_shard_merge(const void* records, int nshards, int B, int K, int V_total, const float* temperature,
+                    const float* top_p, const float* uniforms, int32_t* tokens_out, uint8_t* kept_out,
+                    float* probs_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (nshards < 1 || B < 0 || K < 1 || K > LSS_SHARD_MAX_K || V_total < 1) return LSS_ERR_INVALID_ARG;
+  if ((int64_t)nshards * K > MERGE_CAP) return LSS_ERR_UNSUPPORTED;
+  if (B == 0) return LSS_OK;
+  if (!records || !temperature || !top_p || !uniforms || !tokens_out) return LSS_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < lss_shard_merge_workspace_bytes(B) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return LSS_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  unsigned char* ws = reinterpret_cast<unsigned char*>(workspace);
+  if (cudaMemsetAsync(ws, 0, 256, st) != cudaSuccess) return LSS_ERR_CUDA;
+  if (kept_out && cudaMemsetAsync(kept_out, 0, (size_t)B * V_total, st) != cudaSuccess) return LSS_ERR_CUDA;
+  if (probs_out && cudaMemsetAsync(probs_out, 0, (size_t)B * V_total * sizeof(float), st) != cudaSuccess)
+    return LSS_ERR_CUDA;
+  RowArgs a{};
+  a.B = B;
+  a.V = V_total;
+  a.temperature = temperature;
+  a.top_p = top_p;
+  a.uniforms = uniforms;
+  a.tokens = tokens_out;
+  a.kept_out = kept_out;
+  a.probs_out = probs_out;
+  a.err = reinterpret_cast<uint32_t*>(ws);
+  a.counters = reinterpret_cast<uint32_t*>(ws);
+  a.row_path = reinterpret_cast<int32_t*>(ws + 256);
+  lss_merge_kernel<<<B, NT, 0, st>>>(reinterpret_cast<const unsigned char*>(records), nshards, B, K, a);
+  if (cudaGetLastError() != cudaSuccess) return LSS_ERR_CUDA;
+  return LSS_OK;
 }
 
 int lss_argmax(const void* logits, int dtype, int B, int V, int64_t row_stride, int32_t* tokens_out,
