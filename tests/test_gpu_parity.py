@@ -25,7 +25,7 @@ def check_workload(w, out, rows=None, detail=True):
     worst = 0.0
     stats = {}
     for r in rows:
-        res = R.sample_batch(w, want_detail=detail, rows=[r])[0]
+        res = R.sample_batch(w, want_detail=True, rows=[r])[0]
         path = int(out["paths"][r])
         stats[path] = stats.get(path, 0) + 1
         tok = int(out["tokens"][r])
@@ -212,3 +212,64 @@ def test_chi_square_distribution():
         o2, e2 = o2[:-1], e2[:-1]
     e2 *= o2.sum() / e2.sum()
     assert chisquare(o2, e2).pvalue > 1e-4
+
+
+@needs_cuda
+def test_config4_bf16_all_features():
+    """Config 4 (B=1,024 bf16, every feature on): full detail on every 16th row, and every
+    drawn token inside the oracle's kept set."""
+    w = wl.config4(seed=2)
+    out = G.run(w)
+    assert out["flags"] == 0
+    check_workload(w, out, rows=range(0, w.B, 16))
+    check_workload(w, out, rows=[r for r in range(w.B) if r % 16], detail=False)
+
+
+@needs_cuda
+def test_cuda_graph_capture_and_replay():
+    """prepare + rows captured once in a CUDA graph and replayed on new contents of the same
+    buffers (the decode-loop use), against the oracle for both workloads."""
+    from localstrm_b200 import _lib
+    from localstrm_b200.sampling import BatchSampler
+    w1 = wl.config3(seed=21, B=24, V=32_000, H=300)
+    w2 = wl.config3(seed=22, B=24, V=32_000, H=300)
+    w2.top_k[:] = np.array([0, 5, 50] * 8, np.int32)
+    assert w1.hist_ids.size == w2.hist_ids.size
+    s = BatchSampler("cuda")
+    lib = _lib.load()
+    x, prm, ho, hi, u = G.device_inputs(w1, s.device)
+    tok = torch.empty(w1.B, dtype=torch.int32, device=s.device)
+    H = int(hi.numel())
+    ws = s.workspace(w1.B, w1.V, H)
+    P_ = lambda t: t.data_ptr()
+
+    def step(stream):
+        _lib.check("prepare", lib.lss_sample_prepare(
+            w1.B, w1.V, P_(prm.temperature), P_(prm.top_k), P_(prm.min_p), P_(prm.repetition_penalty),
+            P_(prm.frequency_penalty), P_(prm.presence_penalty), P_(ho), P_(hi), H, P_(ws), ws.numel(), stream))
+        _lib.check("rows", lib.lss_sample_rows(
+            P_(x), 0, w1.B, w1.V, x.stride(0), P_(prm.temperature), P_(prm.top_k), P_(prm.top_p), P_(prm.min_p),
+            P_(prm.repetition_penalty), P_(prm.frequency_penalty), P_(prm.presence_penalty), P_(ho), P_(hi), H,
+            P_(u), P_(tok), None, None, P_(ws), ws.numel(), stream))
+
+    step(torch.cuda.current_stream().cuda_stream)  # warm-up outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step(torch.cuda.current_stream().cuda_stream)
+    for w in (w1, w2, w1):
+        x2, prm2, ho2, hi2, u2 = G.device_inputs(w, s.device)
+        x.copy_(x2)
+        ho.copy_(ho2)
+        hi.copy_(hi2)
+        u.copy_(u2)
+        for name in ("temperature", "top_k", "top_p", "min_p", "repetition_penalty", "frequency_penalty",
+                     "presence_penalty"):
+            getattr(prm, name).copy_(getattr(prm2, name))
+        g.replay()
+        torch.cuda.synchronize()
+        got = tok.cpu().numpy()
+        for r in range(w.B):
+            res = R.sample_batch(w, want_detail=True, rows=[r])[0]
+            if int(got[r]) != res.token:
+                assert res.special == "" and P.draw_is_boundary(res.probs, float(w.uniforms[r])), (r, got[r])
