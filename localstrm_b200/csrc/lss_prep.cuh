@@ -189,20 +189,22 @@ __global__ void __launch_bounds__(HIST_NT) lss_hist_kernel(const HistArgs h) {
   pdl_trigger();  // the scan kernel may launch and start its own set-up
   if (row == 0 && tid < 64) h.header[tid] = 0u;
   if (tid == 0) h.rowflag[row] = 0u;
+  // Every per-row input is requested at once (one round trip), the history offsets included.
   const float T = a.temperature[row];
   const int k = a.top_k[row];
   const float mp = a.min_p[row];
+  const float rp = a.rep[row], fq = a.freq[row], pr = a.pres[row];
+  int b = 0, e = 0;
+  if (a.use_hist) {
+    b = a.hist_off[row];
+    e = a.hist_off[row + 1];
+  }
   const bool bounded = (k > 0 && k < a.V) || (mp > 0.0f && mp < 1.0f) || a.V <= FAST_CAP / 2;
-  const bool active = a.use_hist && T > 0.0f && bounded &&
-                      (a.rep[row] != 1.0f || a.freq[row] != 0.0f || a.pres[row] != 0.0f);
+  const bool active = a.use_hist && T > 0.0f && bounded && (rp != 1.0f || fq != 0.0f || pr != 0.0f);
   const int nseg = h.S;
   int32_t* so = h.seg2 + (int64_t)row * (nseg + 1);
   const PrepOut o{so, h.rowflag + row};
-  int H = 0, b = 0;
-  if (active) {
-    b = a.hist_off[row];
-    H = a.hist_off[row + 1] - b;
-  }
+  const int H = active ? e - b : 0;
   if (!active || H <= 0) {
     if (tid <= nseg) so[tid] = 0;
     return;

@@ -60,7 +60,7 @@ struct __align__(16) ItemScratch {
   uint32_t cnt, flags, pad0, pad1;  // candidates, summary flags
 };
 struct __align__(16) ScanCtl {
-  uint64_t full[SC_NST];        // stage landed (1 arrival + bytes)
+  uint64_t full[SC_NST];        // stage landed (2 arrivals + bytes)
   uint64_t empty[SC_NST];       // stage released (one arrival per compute warp)
   ItemDesc desc[SC_NST];
   ItemScratch sc[2];            // by item parity
@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
   if (tid < (int)(2 * sizeof(ItemScratch) / 4)) reinterpret_cast<uint32_t*>(ctl->sc)[tid] = 0u;  // cnt, flags
   if (tid == 0) {
     for (int q = 0; q < SC_NST; ++q) {
-      mbar_init(&ctl->full[q], 1);
+      mbar_init(&ctl->full[q], 2);  // the logits' arrival, then the history pairs'
       mbar_init(&ctl->empty[q], SC_CW);
     }
     fence_barrier_init();
@@ -148,6 +148,31 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
       }
       cp_async_commit();
     };
+    // The logits of the first SC_NST items stream in while K0 still runs: their copies read
+    // nothing K0 writes (the row parameters are inputs).  Their history arrivals follow below.
+    if (lane < SC_NST) {  // lane j: item j
+      const int j = lane;
+      const int t = blockIdx.x + j * G;
+      if (t < nitems) {
+        const int row = t / S;
+        int slice = t - row * S + row;
+        slice -= (slice / S) * S;
+        const float T = a.temperature[row];
+        const int k = a.top_k[row];
+        const float mp = a.min_p[row];
+        const bool bounded = T <= 0.0f || (k > 0 && k < V) || (mp > 0.0f && mp < 1.0f) || V <= FAST_CAP / 2;
+        const int lo = slice * TS;
+        const int n = min(V, lo + TS) - lo;
+        const char* g0 = reinterpret_cast<const char*>(a.logits) + ((int64_t)row * a.row_stride + lo) * ES;
+        const int nb = (bounded && (reinterpret_cast<uintptr_t>(g0) & 15) == 0) ? ((n * ES) & ~15) : 0;
+        mbar_expect_tx(&ctl->full[j], (uint32_t)nb);
+        unsigned char* dst = smem + j * stage_bytes;
+        constexpr int CH = 32768;
+        for (int off = 0; off < nb; off += CH)
+          bulk_g2s(dst + off, g0 + off, (uint32_t)min(CH, nb - off), &ctl->full[j]);
+      }
+    }
+    __syncwarp();
     pdl_wait();  // K0's pairs and segments are complete and visible
     for (int j = 0; j < SC_AHEAD; ++j) fetch(j);
     for (int j = 0;; ++j) {
@@ -215,11 +240,14 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
         if (j >= SC_NST && !mbar_wait_bounded(&ctl->empty[s], (uint32_t)((j / SC_NST - 1) & 1)))
           atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
         ctl->desc[s] = nd;
-        mbar_expect_tx(&ctl->full[s], (uint32_t)(nd.nb + nd.hbn * 8));
         unsigned char* dst = smem + s * stage_bytes;
-        constexpr int CH = 32768;
-        for (int off = 0; off < nd.nb; off += CH)
-          bulk_g2s(dst + off, g0 + off, (uint32_t)min(CH, nd.nb - off), &ctl->full[s]);
+        if (j >= SC_NST || t >= nitems) {  // the first SC_NST items' logits are in flight already
+          mbar_expect_tx(&ctl->full[s], (uint32_t)nd.nb);
+          constexpr int CH = 32768;
+          for (int off = 0; off < nd.nb; off += CH)
+            bulk_g2s(dst + off, g0 + off, (uint32_t)min(CH, nd.nb - off), &ctl->full[s]);
+        }
+        mbar_expect_tx(&ctl->full[s], (uint32_t)(nd.hbn * 8));
         if (nd.hbn > 0) {
           bulk_g2s(dst + a.tile_bytes, a.uniq_ids + w0, (uint32_t)(nd.hbn * 4), &ctl->full[s]);
           bulk_g2s(dst + a.tile_bytes + SC_HP * 4, a.uniq_cnt + w0, (uint32_t)(nd.hbn * 4), &ctl->full[s]);
