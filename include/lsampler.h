@@ -180,6 +180,22 @@ int lss_sample_noalloc(const void* logits, int dtype, int B, int V, int64_t row_
                        int64_t hist_total, const float* uniforms, int32_t* tokens_out,
                        uint8_t* kept_out, float* probs_out, void* stream);
 
+/* Token-id part of check_stop_criteria (sampling.py:166-196), batched and on the device, so
+ * that a decode loop learns which rows stopped without reading every token back:
+ *   out[b] = LSS_STOP_EOS    when tokens[b] == eos_ids[b] (eos_ids[b] < 0: no EOS id),
+ *            LSS_STOP_TOKEN  else when tokens[b] is one of stop_ids[stop_offsets[b] ..
+ *                            stop_offsets[b+1]),
+ *            LSS_STOP_NONE   otherwise.
+ * The reference checks the EOS id first, then the stop ids (sampling.py:182-185).  The
+ * stop-string part (:188-194) needs the tokenizer and stays on the host.  eos_ids may be NULL
+ * (no EOS ids); stop_offsets NULL means no stop ids (stop_ids is then ignored).  All pointers
+ * are device pointers; asynchronous on `stream`. */
+#define LSS_STOP_NONE 0
+#define LSS_STOP_EOS 1
+#define LSS_STOP_TOKEN 2
+int lss_stop_check(const int32_t* tokens, int B, const int32_t* eos_ids, const int32_t* stop_offsets,
+                   const int32_t* stop_ids, int32_t* out, void* stream);
+
 /* Synchronises `stream`, then returns the device error flags accumulated in the
  * workspace since lss_sample last cleared them (0 when none). */
 int lss_read_status(const void* workspace, uint32_t* flags_out, void* stream);

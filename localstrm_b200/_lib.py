@@ -60,6 +60,8 @@ def _declare(lib: ctypes.CDLL) -> None:
                                        c_int64, P, P, P, P, P]
     lib.lss_argmax.restype = c_int
     lib.lss_argmax.argtypes = [P, c_int, c_int, c_int, c_int64, P, P]
+    lib.lss_stop_check.restype = c_int
+    lib.lss_stop_check.argtypes = [P, c_int, P, P, P, P, P]
     lib.lss_read_status.restype = c_int
     lib.lss_read_status.argtypes = [P, ctypes.POINTER(c_uint32), P]
     lib.lss_read_row_paths.restype = c_int

@@ -94,6 +94,28 @@ __global__ void __launch_bounds__(NT) lss_argmax_kernel(const void* logits, int6
 
 
 // ---------------------------------------------------------------------------
+// Stop check: the token-id part of check_stop_criteria (sampling.py:182-185), one thread per
+// row: the EOS id first, then the row's stop ids.
+// ---------------------------------------------------------------------------
+__global__ void lss_stop_kernel(const int32_t* tokens, int B, const int32_t* eos_ids, const int32_t* stop_off,
+                                const int32_t* stop_ids, int32_t* out) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int32_t t = tokens[b];
+  int32_t code = LSS_STOP_NONE;
+  if (eos_ids && eos_ids[b] >= 0 && t == eos_ids[b]) {
+    code = LSS_STOP_EOS;
+  } else if (stop_off) {
+    for (int i = stop_off[b], e = stop_off[b + 1]; i < e; ++i)
+      if (stop_ids[i] == t) {
+        code = LSS_STOP_TOKEN;
+        break;
+      }
+  }
+  out[b] = code;
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 constexpr int TILE_TARGET_BYTES = 80 * 1024;   // second kernel: slice size per CTA
@@ -698,6 +720,18 @@ int lss_argmax(const void* logits, int dtype, int B, int V, int64_t row_stride, 
     cudaGetLastError();
     return LSS_ERR_CUDA;
   }
+  return LSS_OK;
+}
+
+int lss_stop_check(const int32_t* tokens, int B, const int32_t* eos_ids, const int32_t* stop_offsets,
+                   const int32_t* stop_ids, int32_t* out, void* stream) {
+  if (B < 0) return LSS_ERR_INVALID_ARG;
+  if (B == 0) return LSS_OK;
+  if (!tokens || !out || (stop_offsets && !stop_ids)) return LSS_ERR_INVALID_ARG;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  constexpr int T = 256;
+  lss_stop_kernel<<<(unsigned)((B + T - 1) / T), T, 0, st>>>(tokens, B, eos_ids, stop_offsets, stop_ids, out);
+  if (cudaGetLastError() != cudaSuccess) return LSS_ERR_CUDA;
   return LSS_OK;
 }
 

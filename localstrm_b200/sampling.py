@@ -20,7 +20,7 @@ from __future__ import annotations
 
 import ctypes
 from dataclasses import dataclass, field
-from typing import List, Optional, Sequence, Union
+from typing import List, Optional, Sequence, Tuple, Union
 
 import numpy as np
 import torch
@@ -277,6 +277,74 @@ def sample_next_token(logits: torch.Tensor, params: SamplingParams,
     hist = [past_token_ids] if past_token_ids else None
     tok = sample_batch(row, [params], hist)
     return int(tok.item())
+
+
+STOP_NONE, STOP_EOS, STOP_TOKEN = 0, 1, 2
+
+
+def check_stop_batch(tokens: torch.Tensor, eos_token_id=None,
+                     stop_token_ids: Optional[Sequence] = None) -> torch.Tensor:
+    """Token-id part of ``check_stop_criteria`` (``sampling.py:182-185``) for a CUDA batch of
+    freshly sampled ids, on the device: an int32 code per row, ``STOP_EOS`` when the token is
+    the row's EOS id, else ``STOP_TOKEN`` when it is one of the row's stop ids, else
+    ``STOP_NONE``.
+
+    ``eos_token_id``: one id for every row, a per-row sequence (``None`` or a negative id: no
+    EOS id), or ``None``.  ``stop_token_ids``: one list for every row or one list per row.
+    The stop-string part (``sampling.py:188-194``) needs the tokenizer and stays on the host.
+    """
+    if not isinstance(tokens, torch.Tensor) or not tokens.is_cuda or tokens.dim() != 1:
+        raise ValueError("tokens must be a 1-D CUDA tensor")
+    dev = tokens.device
+    tok = tokens.to(torch.int32).contiguous()
+    B = tok.numel()
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+    eos = None
+    if eos_token_id is not None:
+        if isinstance(eos_token_id, (int, np.integer)):
+            e = np.full(B, int(eos_token_id), dtype=np.int32)
+        else:
+            vals = list(eos_token_id)
+            if len(vals) != B:
+                raise ValueError(f"expected {B} EOS ids, got {len(vals)}")
+            e = np.array([-1 if v is None else int(v) for v in vals], dtype=np.int32)
+        eos = torch.from_numpy(e).to(dev)
+    offs = ids = None
+    if stop_token_ids is not None:
+        lists = list(stop_token_ids)
+        if lists and not isinstance(lists[0], (list, tuple, np.ndarray)):
+            lists = [lists] * B  # one list for every row
+        if len(lists) != B:
+            raise ValueError(f"expected {B} stop-id lists, got {len(lists)}")
+        o = np.zeros(B + 1, dtype=np.int32)
+        for r, l in enumerate(lists):
+            o[r + 1] = o[r] + len(l)
+        flat = np.array([int(i) for l in lists for i in l], dtype=np.int32)
+        offs = torch.from_numpy(o).to(dev)
+        ids = torch.from_numpy(flat if flat.size else np.zeros(1, np.int32)).to(dev)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    P = lambda t: t.data_ptr() if t is not None else None
+    _lib.check("lss_stop_check", lib.lss_stop_check(tok.data_ptr(), B, P(eos), P(offs), P(ids),
+                                                    out.data_ptr(), stream))
+    return out
+
+
+def stop_reasons(codes, tokens) -> List[Tuple[bool, Optional[str]]]:
+    """The reference's ``(should_stop, reason)`` per row (``sampling.py:182-185``) from the
+    codes of ``check_stop_batch``; rows with ``STOP_NONE`` still owe the host stop-string
+    check."""
+    c = codes.tolist() if isinstance(codes, torch.Tensor) else list(codes)
+    t = tokens.tolist() if isinstance(tokens, torch.Tensor) else list(tokens)
+    out = []
+    for code, tk in zip(c, t):
+        if code == STOP_EOS:
+            out.append((True, "eos_token"))
+        elif code == STOP_TOKEN:
+            out.append((True, f"stop_token_{tk}"))
+        else:
+            out.append((False, None))
+    return out
 
 
 def apply_top_k_top_p_min_p(logits: torch.Tensor, top_k: int = -1, top_p: float = 1.0,

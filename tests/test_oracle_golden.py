@@ -78,3 +78,18 @@ def test_ordered_key_is_monotone():
     order_v = np.argsort(v, kind="stable")
     assert np.all(np.diff(k[order_v].astype(np.int64)) >= 0)
     assert R.ordered_key(np.float32(-0.0)) == R.ordered_key(np.float32(0.0))
+
+
+def _stop_cases():
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "stop_check.npz"))
+    lists = [g["ids"][g["offsets"][i]:g["offsets"][i + 1]] for i in range(len(g["tokens"]))]
+    return g, lists
+
+
+def test_stop_code_matches_reference():
+    """The restated token-id stop check against check_stop_criteria's own results."""
+    g, lists = _stop_cases()
+    for i, t in enumerate(g["tokens"]):
+        eos = None if g["eos"][i] < 0 else int(g["eos"][i])
+        assert R.stop_code(int(t), eos, [int(v) for v in lists[i]]) == int(g["codes"][i]), i
