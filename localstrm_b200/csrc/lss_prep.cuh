@@ -248,15 +248,16 @@ __global__ void __launch_bounds__(HIST_NT) lss_hist_kernel(const HistArgs h) {
       atomicOr(o.bad, LSS_FLAG_BAD_HISTORY);
       id = -1;
     }
-    const unsigned same = __match_any_sync(0xffffffffu, id);
+    // Every lane inserts its own id: merging equal ids across the warp first (match.any)
+    // cost more time than the atomics it saves.
     bool fresh = false;
     uint32_t slot = 0;
-    if (id >= 0 && lane == __ffs(same) - 1) {
+    if (id >= 0) {
       uint32_t hh = ((uint32_t)id * 2654435761u) & (cap - 1);
       for (uint32_t probe = 0; probe < cap; ++probe) {
         const uint32_t old = atomicCAS(&keys[hh], EMPTY, (uint32_t)id);
         if (old == EMPTY || old == (uint32_t)id) {
-          atomicAdd(&cnts[hh], (uint32_t)__popc(same));
+          atomicAdd(&cnts[hh], 1u);
           fresh = old == EMPTY;
           slot = hh;
           break;
@@ -270,11 +271,9 @@ __global__ void __launch_bounds__(HIST_NT) lss_hist_kernel(const HistArgs h) {
       uint32_t base = 0;
       if (lane == leader) base = atomicAdd(nlist, (uint32_t)__popc(bal));
       base = __shfl_sync(0xffffffffu, base, leader);
-      const int c = fresh ? (int)((uint32_t)id / TS) : -1;
-      const unsigned sc = __match_any_sync(0xffffffffu, c);
       if (fresh) {
         slist[base + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)slot;
-        if (lane == __ffs(sc) - 1) atomicAdd(&bcnt[c], (uint32_t)__popc(sc));
+        atomicAdd(&bcnt[(uint32_t)id / TS], 1u);
       }
     }
   }
