@@ -50,16 +50,56 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples while the timed region runs."""
+    """SM clock and throttle-reason samples taken while the timed region runs: NVML polled every
+    2 ms from a thread (``nvidia-smi -lms 100`` when NVML is unavailable)."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.thread = None
+        self.nv = None
+        self.handle = None
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = None
+            try:  # the NVML device of this CUDA device, by PCI bus
+                prop = torch.cuda.get_device_properties(gpu_index)
+                bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+                h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                h = nv.nvmlDeviceGetHandleByIndex(gpu_index)
+            self.nv, self.handle = nv, h
+        except Exception:
+            self.nv = None
+
+    def _poll(self):
+        nv, h = self.nv, self.handle
+        bits = {"hw_slowdown": nv.nvmlClocksThrottleReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksThrottleReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksThrottleReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksThrottleReasonSwPowerCap}
+        while not self.stop_flag:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+                r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.samples.append((float(sm), float(mx), {n for n, b in bits.items() if r & b}))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def start(self):
+        if self.nv is not None:
+            import threading
+            self.samples, self.stop_flag = [], False
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
@@ -68,31 +108,40 @@ class ClockSampler:
             self.proc = None
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
         sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
+        if self.thread is not None:
+            self.stop_flag = True
+            self.thread.join()
+            for a, b, r in self.samples:
+                sm.append(a)
+                mx.append(b)
+                reasons |= r
+            src = "nvml, 2 ms"
+        elif self.proc is not None:
+            self.proc.terminate()
             try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            for line in out.strip().splitlines():
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    mx.append(float(f[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(self.NAMES, f[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+            src = "nvidia-smi, 100 ms"
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"]}
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": src}
 
 
 def cpu_reference_rate(w, seconds: float = 12.0, min_rows: int = 8):
@@ -223,7 +272,6 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     barrier()
     torch.cuda.synchronize()
     clocks.start()
-    time.sleep(0.3)
     # The timed steps run back to back, as a decode loop replays them: two events bracket the
     # whole run, none sits between the steps.
     reps = max(1, args.inner)
@@ -371,7 +419,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--inner", type=int, default=1, help="calls per timed step")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
