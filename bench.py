@@ -32,7 +32,24 @@ sys.path.insert(0, ROOT)
 METRIC = "sampled rows/s & HBM GB/s vs peak at B=256 V=151936; 1/2/4/8 GPU"
 B_PER_GPU = 256
 V = 151_936
-NBUF = 4  # rotating input buffers: 4 x 155.6 MB > L2 (126 MB), so every step reads cold
+L2_BYTES = 126e6
+TORCH_DT = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
+DT_CODE = {"f32": 0, "bf16": 1, "f16": 2}
+WORKLOADS = ("headline", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5")
+DESC = {
+    "headline": "headline: B=256 rows/GPU, V=151936 f32 logits, T0.7 p0.95 mp0.05 rep1.1 freq0.3 pres0.2, H=2048",
+    "cfg1": "config 1: B=8 rows/GPU, V=151936 f32, 2 greedy + 6 T0.8/k50/p0.9",
+    "cfg2": "config 2: B=64 rows/GPU, V=151936 bf16, per-row T/k/p/min-p, rep1.1, H=512",
+    "cfg3": "config 3: B=256 rows/GPU, V=128256 f32, T0.7 p0.95 mp0.05 rep1.1 freq0.3 pres0.2, H=2048",
+    "cfg4": "config 4: B=1024 rows split over the GPUs, V=151936 bf16, every feature on",
+    "cfg5": "config 5: B=128, V=256000 f32 split by columns over the GPUs, T1.0 top-k 64 (records) p0.9",
+}
+
+
+def n_buffers(buf_bytes: float) -> int:
+    """Rotating input buffers: enough that one pass over them exceeds twice the L2, so every
+    step reads its logits from HBM."""
+    return int(min(64, max(4, -(-2 * L2_BYTES // buf_bytes))))
 
 
 def algorithmic_bytes(w) -> int:
@@ -160,15 +177,38 @@ def cpu_reference_rate(w, seconds: float = 12.0, min_rows: int = 8):
     return n / dt, threads, n, dt
 
 
-def make_workload(rank: int):
+def _row_block(w, start: int, stop: int):
+    """Rows [start, stop) of a workload, histories re-based."""
+    import copy
+    b = copy.copy(w)
+    o = w.hist_offsets
+    b.logits = w.logits[start:stop]
+    for f in ("temperature", "top_k", "top_p", "min_p", "repetition_penalty", "frequency_penalty",
+              "presence_penalty", "uniforms"):
+        setattr(b, f, getattr(w, f)[start:stop])
+    b.hist_ids = w.hist_ids[o[start]:o[stop]]
+    b.hist_offsets = (o[start:stop + 1] - o[start]).astype(np.int32)
+    return b
+
+
+def make_workload(rank: int, world: int = 1, name: str = "headline"):
+    """The rank's rows of a row-mode workload; config 4's 1,024 rows are split over the ranks
+    (strong scaling), every other workload gives each rank its own batch (weak scaling)."""
     from localstrm_b200 import workloads as wl
-    return wl.headline(seed=rank, B=B_PER_GPU, V=V)
+    from localstrm_b200.distributed import shard_rows
+    if name == "headline":
+        return wl.headline(seed=rank, B=B_PER_GPU, V=V)
+    if name == "cfg4":
+        full = wl.config4(seed=0)
+        a, b = shard_rows(full.B, world, rank)
+        return _row_block(full, a, b)
+    return {"cfg1": wl.config1, "cfg2": wl.config2, "cfg3": wl.config3}[name](seed=rank)
 
 
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return
-    w = make_workload(0)
+    w = make_workload(0, 1, args.workload) if args.workload != "cfg5" else _cfg5_full()
     rates = []
     meta = None
     for i in range(args.warmup + args.steps):
@@ -182,10 +222,9 @@ def run_reference(args, rank: int, world: int):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * B_PER_GPU / value, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; config 3 distribution)",
-        "config": {"workload": "headline: B=256 V=151936 f32, config-3 params", "global_batch": B_PER_GPU,
-                   "parallelism": "cpu"},
+        "ms_per_step": 1000.0 * w.B / value, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": w.dtype, "data": "synthetic (seeded)",
+        "config": {"workload": DESC[args.workload], "global_batch": w.B, "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": cores, "kind": "port",
                          "sample": f"{n} rows of the workload per step (~{dt:.1f} s), per-row "
                                    "sample_next_token restated in torch CPU ops"},
@@ -202,9 +241,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     lib = _lib.load()
-    w = make_workload(rank)
+    w = make_workload(rank, world, args.workload)
     B = w.B
-    logits_host = torch.from_numpy(w.logits).pin_memory()
+    DTC = DT_CODE[w.dtype]
+    logits_host = torch.from_numpy(w.logits).to(TORCH_DT[w.dtype]).pin_memory()
+    NBUF = n_buffers(logits_host.numel() * logits_host.element_size())
     bufs = [logits_host.to(dev) for _ in range(NBUF)]
     prm = RowParams.from_arrays(dev, temperature=w.temperature, top_k=w.top_k, top_p=w.top_p,
                                 min_p=w.min_p, repetition_penalty=w.repetition_penalty,
@@ -227,7 +268,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             ws.numel(), sp))
 
     def rows(x, sp, scan_only=False):
-        args_ = (P(x), 0, B, w.V, x.stride(0), P(prm.temperature), P(prm.top_k), P(prm.top_p),
+        args_ = (P(x), DTC, B, w.V, x.stride(0), P(prm.temperature), P(prm.top_k), P(prm.top_p),
                  P(prm.min_p), P(prm.repetition_penalty), P(prm.frequency_penalty),
                  P(prm.presence_penalty), P(h_off), P(h_ids), H, P(uni), P(tokens))
         if scan_only:
@@ -325,7 +366,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     peak, peak_kind = peaks()
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tp):
+    if args.workload == "headline" and os.path.exists(tp):
         try:
             traffic = json.load(open(tp)).get("lss_scan_kernel_headline_bytes_per_launch")
         except (OSError, ValueError):
@@ -343,7 +384,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                               "frequency_penalty", "presence_penalty")}
         dev_x = torch.empty_like(bufs[0])
         tok_host = torch.empty(B * world, dtype=torch.int32).pin_memory()
-        h2d = logits_host.numel() * 4 + host_u.numel() * 4 + host_off.numel() * 4 + \
+        h2d = logits_host.numel() * logits_host.element_size() + host_u.numel() * 4 + host_off.numel() * 4 + \
             host_ids.numel() * 4 + sum(t.numel() * 4 for t in host_prm.values())
         d2h = tok_host.numel() * 4 if rank == 0 else B * 4
 
@@ -390,17 +431,20 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     paths = s.row_paths(B)
     flags = s.status()
+    global_b = B * world
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded; config 3 distribution at V=151,936)",
-            "config": {"workload": "headline: B=256 rows/GPU, V=151936 f32 logits, T0.7 p0.95 "
-                                   "mp0.05 rep1.1 freq0.3 pres0.2, H=2048",
-                       "global_batch": B * world, "rows_per_gpu": B, "vocab": w.V,
+            "higher_is_better": True, "scaling": "strong" if args.workload == "cfg4" else "weak",
+            "vs_baseline": None, "dtype": w.dtype,
+            "data": "synthetic (seeded; " + ("config 3 distribution at V=151,936)" if args.workload == "headline"
+                                             else f"{args.workload})"),
+            "config": {"workload": DESC[args.workload],
+                       "global_batch": global_b, "rows_per_gpu": B, "vocab": w.V,
                        "parallelism": f"rows{world}" if world > 1 else "single",
-                       "l2": f"{NBUF} rotating input buffers of {B * w.V * 4 / 1e6:.1f} MB (> 126 MB L2)",
+                       "l2": f"{NBUF} rotating input buffers of {logits_host.numel() * logits_host.element_size() / 1e6:.1f} MB"
+                             f" (together > 2 x 126 MB L2)",
                        "inner_reps": reps},
             "hbm_gbs": alg * world * n_steps_total / (elapsed_ms / 1000.0) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -416,6 +460,110 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         print(json.dumps(line), flush=True)
 
 
+def _cfg5_full():
+    from localstrm_b200 import workloads as wl
+    return wl.config5(seed=0)
+
+
+def run_vocab(args, rank: int, world: int, local_rank: int):
+    """Config 5, vocabulary-sharded: every rank holds a column block of all 128 rows; a step is
+    the shard records (lss_shard_topk), one all-gather of the records, and the merge and draw
+    (lss_shard_merge) on every rank.  Timed eagerly with events (the collective is not captured)."""
+    import torch.distributed as dist
+    from localstrm_b200 import _lib
+    from localstrm_b200.distributed import shard_vocab
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+    w = _cfg5_full()
+    B, Vt, K = w.B, w.V, 64
+    off, end = shard_vocab(Vt, world, rank)
+    Vs = end - off
+    shard_host = torch.from_numpy(np.ascontiguousarray(w.logits[:, off:end])).pin_memory()
+    nbuf = n_buffers(shard_host.numel() * 4)
+    bufs = [shard_host.to(dev) for _ in range(nbuf)]
+    T = torch.from_numpy(w.temperature).to(dev)
+    tp = torch.from_numpy(w.top_p).to(dev)
+    u = torch.from_numpy(w.uniforms).to(dev)
+    rb = int(lib.lss_shard_record_bytes(K))
+    rec = torch.empty(B * rb, dtype=torch.uint8, device=dev)
+    gathered = torch.empty(world * B * rb, dtype=torch.uint8, device=dev)
+    mws = torch.empty(int(lib.lss_shard_merge_workspace_bytes(B)), dtype=torch.uint8, device=dev)
+    tok = torch.empty(B, dtype=torch.int32, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def records(x):
+        _lib.check("lss_shard_topk", lib.lss_shard_topk(x.data_ptr(), 0, B, Vs, x.stride(0), off, T.data_ptr(),
+                                                        K, rec.data_ptr(), st.cuda_stream))
+
+    def step(i):
+        records(bufs[i % nbuf])
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, rec)
+            src = gathered
+        else:
+            src = rec
+        _lib.check("lss_shard_merge", lib.lss_shard_merge(src.data_ptr(), world, B, K, Vt, T.data_ptr(),
+                                                          tp.data_ptr(), u.data_ptr(), tok.data_ptr(), None, None,
+                                                          mws.data_ptr(), mws.numel(), st.cuda_stream))
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(args.steps):
+        step(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # the shard kernel alone (the dominant kernel), events around each launch
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        kev[i][0].record(st)
+        records(bufs[i % nbuf])
+        kev[i][1].record(st)
+    torch.cuda.synchronize()
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    alg = B * Vs * 4 + B * rb
+    peak, peak_kind = peaks()
+    achieved = alg / (kern_ms / 1000.0) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        rate, cores, n, dt = cpu_reference_rate(w, seconds=args.cpu_seconds)
+        cpu = {"value": rate, "unit": "rows/s", "cores": cores, "kind": "port",
+               "sample": f"{n} whole rows (~{dt:.1f} s): per-row sample_next_token with top-k 64, top-p 0.9 "
+                         f"restated in torch CPU ops (oracle/torch_port.py)"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": B * args.steps / (ms / 1000.0), "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; cfg5)",
+            "config": {"workload": DESC["cfg5"], "global_batch": B, "vocab": Vt, "vocab_per_gpu": Vs,
+                       "parallelism": f"vocab{world}", "records_bytes_per_rank": B * rb,
+                       "l2": f"{nbuf} rotating shard buffers of {shard_host.numel() * 4 / 1e6:.1f} MB"
+                             f" (together > 2 x 126 MB L2)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "kernel": "lss_shard_kernel",
+                         "peak_source": peak_kind, "algorithmic_bytes_per_launch": alg, "kernel_ms": kern_ms},
+            "clocks": clk, "e2e": None, "cpu_baseline": cpu, "gpu_launches": 2 * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -425,6 +573,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--workload", default="headline", choices=WORKLOADS,
+                    help="headline (the metric point) or one of the other configurations")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -443,7 +593,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.workload == "cfg5":
+            run_vocab(args, rank, world, local_rank)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
