@@ -295,10 +295,12 @@ static cudaError_t launch_rows(const ScanArgs& sa, const RowArgs& ra, const Gath
                                cudaStream_t st, bool scan_only) {
   static KernelCfg scan_cfg{};
   int nctas = 0;
-  cudaError_t e = prepare_scan_kernel(lss_scan_kernel<DT>, scan_cfg, pl.scan_smem, nctas);
+  // 16-bit logits: half-size stages plus an f32 work tile (the same total as f32 stages).
+  const int smem = DT == LSS_DTYPE_F32 ? pl.scan_smem : scan_smem_bytes(sa.tile_bytes, sa.work_bytes);
+  cudaError_t e = prepare_scan_kernel(lss_scan_kernel<DT>, scan_cfg, smem, nctas);
   if (e != cudaSuccess) return e;
   const int nitems = B * pl.S;
-  e = launch_pdl(lss_scan_kernel<DT>, (unsigned)std::min(nctas, nitems), (unsigned)SC_NT, (size_t)pl.scan_smem, 1,
+  e = launch_pdl(lss_scan_kernel<DT>, (unsigned)std::min(nctas, nitems), (unsigned)SC_NT, (size_t)smem, 1,
                  st, sa);
   if (e != cudaSuccess || scan_only) return e;
   e = launch_pdl(lss_resolve_kernel, (unsigned)B, (unsigned)NT, (size_t)0, 1, st, ra, ga);
@@ -476,7 +478,13 @@ static int sample_rows(const void* logits, int dtype, int B, int V, int64_t row_
   sa.S = pl.S;
   sa.TS = pl.TS;
   sa.SEG = pl.SEG;
-  sa.tile_bytes = pl.scan_tile;
+  if (dtype == LSS_DTYPE_F32) {
+    sa.tile_bytes = pl.scan_tile;
+    sa.work_bytes = 0;
+  } else {
+    sa.tile_bytes = round_up(pl.TS * 2, 128);
+    sa.work_bytes = pl.scan_tile;  // TS f32 values
+  }
   sa.use_hist = hist_total > 0 ? 1 : 0;
   sa.temperature = temperature;
   sa.top_k = top_k;

@@ -62,7 +62,7 @@ struct __align__(16) ItemScratch {
 struct __align__(16) ScanCtl {
   uint64_t full[SC_NST];        // stage landed (2 arrivals + bytes)
   uint64_t empty[SC_NST];       // stage released (one arrival per compute warp)
-  ItemDesc desc[SC_NST];
+  ItemDesc desc[2 * SC_NST];   // by item (j % 4): a released stage's next item does not overwrite it
   ItemScratch sc[2];            // by item parity
   uint64_t best[2][32];         // greedy items: argmax code per warp
   uint32_t wkey[2][32];         // sampled items: max key of z per warp (all ones: NaN / +inf)
@@ -74,6 +74,7 @@ struct ScanArgs {
   int64_t row_stride;
   int B, V, S, TS, SEG;
   int tile_bytes;               // tile part of a stage (multiple of 128 bytes)
+  int work_bytes;               // 16-bit logits: the f32 work tile they are widened into (else 0)
   int use_hist;
   const float* temperature;
   const int32_t* top_k;
@@ -91,8 +92,8 @@ struct ScanArgs {
 };
 
 __host__ __device__ constexpr int scan_stage_bytes(int tile_bytes) { return tile_bytes + SC_HB * 4; }
-__host__ __device__ constexpr int scan_smem_bytes(int tile_bytes) {
-  return SC_NST * scan_stage_bytes(tile_bytes) + (((NBIN + 1) * 4 + 15) & ~15) +
+__host__ __device__ constexpr int scan_smem_bytes(int tile_bytes, int work_bytes = 0) {
+  return SC_NST * scan_stage_bytes(tile_bytes) + work_bytes + (((NBIN + 1) * 4 + 15) & ~15) +
          (int)((sizeof(ScanCtl) + 15) & ~15);
 }
 
@@ -103,8 +104,10 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
   constexpr int ES = DT == LSS_DTYPE_F32 ? 4 : 2;
   extern __shared__ __align__(1024) unsigned char smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr bool W16 = DT != LSS_DTYPE_F32;  // 16-bit logits: widened into a separate f32 tile
   const int stage_bytes = scan_stage_bytes(a.tile_bytes);
-  uint32_t* HL = reinterpret_cast<uint32_t*>(smem + SC_NST * stage_bytes);
+  float* WT = reinterpret_cast<float*>(smem + SC_NST * stage_bytes);  // work tile (16-bit logits)
+  uint32_t* HL = reinterpret_cast<uint32_t*>(smem + SC_NST * stage_bytes + a.work_bytes);
   ScanCtl* ctl = reinterpret_cast<ScanCtl*>(reinterpret_cast<unsigned char*>(HL) + (((NBIN + 1) * 4 + 15) & ~15));
   const int V = a.V, S = a.S, TS = a.TS;
   const int nitems = a.B * S;
@@ -239,7 +242,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
         }
         if (j >= SC_NST && !mbar_wait_bounded(&ctl->empty[s], (uint32_t)((j / SC_NST - 1) & 1)))
           atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
-        ctl->desc[s] = nd;
+        ctl->desc[j % (2 * SC_NST)] = nd;
         unsigned char* dst = smem + s * stage_bytes;
         if (j >= SC_NST || t >= nitems) {  // the first SC_NST items' logits are in flight already
           mbar_expect_tx(&ctl->full[s], (uint32_t)nd.nb);
@@ -274,76 +277,60 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
     if (DT == LSS_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(g0)[i]);
     return __half2float(reinterpret_cast<const __half*>(g0)[i]);
   };
-  bool wrote = false;  // this thread wrote the stage through the generic proxy
+  bool wrote = false;     // this thread wrote the stage through the generic proxy
+  bool released = false;  // the warp released the current item's stage in the preparation
   // Waits for item jj's stage and prepares it; false at the end of the list (uniform).
   auto prepare = [&](int jj) -> bool {
     const int s = jj % SC_NST;
     if (!mbar_wait_bounded_sleep(&ctl->full[s], (uint32_t)((jj / SC_NST) & 1)) && ctid == 0)
       atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
-    const ItemDesc& D = ctl->desc[s];
+    const ItemDesc& D = ctl->desc[jj % (2 * SC_NST)];
     const int mode = D.mode;
     wrote = false;
+    released = false;
     if (mode == ITEM_END) return false;
     if (mode == ITEM_SKIP) return true;
     const int row = D.row, lo = D.lo, n = D.n;
     const int n4 = (n + 3) >> 2;
-    float* tile = reinterpret_cast<float*>(smem + s * stage_bytes);
+    // f32: the values are used in the stage; 16-bit: widened into the work tile, which the
+    // bulk copies never write, so the stage is only read and is released below, right after.
+    float* tile = W16 ? WT : reinterpret_cast<float*>(smem + s * stage_bytes);
     const char* g0 = reinterpret_cast<const char*>(a.logits) + ((int64_t)row * a.row_stride + lo) * ES;
     const int nbulk = D.nb / ES;
-    // ---- what the bulk copy skipped (ragged tail / unaligned rows), widening, padding
-    float tailv = 0.0f;
-    const int ntail = n - nbulk;
-    if (DT == LSS_DTYPE_F32 || nbulk == 0) {
-      for (int i = nbulk + ctid; i < n; i += SC_CT) {
-        tile[i] = load_elem(g0, i);
-        wrote = true;
-      }
-    } else if (ctid < ntail) {
-      tailv = load_elem(g0, nbulk + ctid);
-    }
-    if (DT != LSS_DTYPE_F32 && nbulk > 0) {
-      // Widen in place, back to front: chunk c's f32 writes only overwrite 16-bit data of
-      // chunks >= 2c, which earlier iterations consumed.
-      const uint16_t* h = reinterpret_cast<const uint16_t*>(tile);
-      constexpr int W = SC_CT * 8;
-      const int nch = (nbulk + W - 1) / W;
-      for (int c = nch - 1; c >= 0; --c) {
-        const int i0 = c * W + ctid * 8;
+    // ---- widening, what the bulk copy skipped (ragged tail / unaligned rows), padding
+    if (W16 && nbulk > 0) {
+      const uint16_t* h = reinterpret_cast<const uint16_t*>(smem + s * stage_bytes);
+      for (int i0 = ctid * 8; i0 < nbulk; i0 += SC_CT * 8) {  // nbulk is a multiple of 8
+        const uint4 raw = *reinterpret_cast<const uint4*>(h + i0);
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
         float v[8];
-        const bool act = i0 < nbulk;
-        if (act) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(h + i0);
-          const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            if (DT == LSS_DTYPE_BF16) {
-              v[2 * q] = __uint_as_float(w[q] << 16);
-              v[2 * q + 1] = __uint_as_float(w[q] & 0xffff0000u);
-            } else {
-              v[2 * q] = __half2float(__ushort_as_half((uint16_t)(w[q] & 0xffffu)));
-              v[2 * q + 1] = __half2float(__ushort_as_half((uint16_t)(w[q] >> 16)));
-            }
+        for (int q = 0; q < 4; ++q) {
+          if (DT == LSS_DTYPE_BF16) {
+            v[2 * q] = __uint_as_float(w[q] << 16);
+            v[2 * q + 1] = __uint_as_float(w[q] & 0xffff0000u);
+          } else {
+            v[2 * q] = __half2float(__ushort_as_half((uint16_t)(w[q] & 0xffffu)));
+            v[2 * q + 1] = __half2float(__ushort_as_half((uint16_t)(w[q] >> 16)));
           }
         }
-        sc_sync();
-        if (act) {
-          float4* dd = reinterpret_cast<float4*>(tile + i0);
-          dd[0] = make_float4(v[0], v[1], v[2], v[3]);
-          dd[1] = make_float4(v[4], v[5], v[6], v[7]);
-          wrote = true;
-        }
+        float4* dd = reinterpret_cast<float4*>(tile + i0);
+        dd[0] = make_float4(v[0], v[1], v[2], v[3]);
+        dd[1] = make_float4(v[4], v[5], v[6], v[7]);
       }
-      sc_sync();
-      if (ctid < ntail) tile[nbulk + ctid] = tailv;
+    }
+    for (int i = nbulk + ctid; i < n; i += SC_CT) {
+      tile[i] = load_elem(g0, i);
+      if (!W16) wrote = true;
     }
     if (ctid < n4 * 4 - n) {
       tile[n + ctid] = -INFINITY;
-      wrote = true;
+      if (!W16) wrote = true;
     }
     // ---- history penalties (sampling.py:55-66), once per unique id of the slice
     const int np = D.hcount;
     // Entries written above by other threads (plain loads, widening) are complete first.
-    if (np > 0 && (nbulk < n || DT != LSS_DTYPE_F32)) sc_sync();
+    if (np > 0 && (nbulk < n || W16)) sc_sync();
     if (np > 0) {
       const int32_t* ids = reinterpret_cast<const int32_t*>(smem + s * stage_bytes + a.tile_bytes);
       const int32_t* cnt = ids + SC_HP;
@@ -354,8 +341,13 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
         const int id = w < hbn ? ids[w] : a.uniq_ids[hb + e];
         const int c = w < hbn ? cnt[w] : a.uniq_cnt[hb + e];
         tile[id - lo] = penalise(tile[id - lo], rp, fq, pr, c);
-        wrote = true;
+        if (!W16) wrote = true;
       }
+    }
+    if (W16) {  // this warp has read all it needs of the stage (values and pairs)
+      __syncwarp();
+      if (lane == 0) mbar_arrive_local(&ctl->empty[s]);
+      released = true;
     }
     return true;
   };
@@ -384,12 +376,12 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
   for (int j = 0;; ++j) {
     const int s = j % SC_NST, ip = j & 1;  // stage, item parity (scratch)
     ItemScratch* sc = &ctl->sc[ip];
-    const ItemDesc& D = ctl->desc[s];
+    const ItemDesc& D = ctl->desc[j % (2 * SC_NST)];
     sc_sync();  // item j: slice and history counts complete; item j-1 done by every warp
     if (warp == 0) write_summary();
     const int mode = D.mode;
     const int lo = D.lo, n = D.n, n4 = (n + 3) >> 2;
-    const float4* t4 = reinterpret_cast<const float4*>(smem + s * stage_bytes);
+    const float4* t4 = reinterpret_cast<const float4*>(W16 ? reinterpret_cast<unsigned char*>(WT) : smem + s * stage_bytes);
     const int k = D.k;
     float4 v[SC_R];
     float tmax = -INFINITY;  // max of this thread's values
@@ -429,9 +421,11 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
     // stage released, so that the next copy into it starts now.
     const int row = D.row, slice = D.slice;
     const float T = D.T, tl = D.tl, sbin = D.sb, binw = D.binw;
-    if (wrote) fence_proxy_async();  // generic writes to the stage precede the next bulk copy
-    __syncwarp();
-    if (lane == 0) mbar_arrive_local(&ctl->empty[s]);
+    if (!released) {
+      if (wrote) fence_proxy_async();  // generic writes to the stage precede the next bulk copy
+      __syncwarp();
+      if (lane == 0) mbar_arrive_local(&ctl->empty[s]);
+    }
     sc_sync();
 
     // ---- X(j)
