@@ -5,7 +5,10 @@ distribution (Gumbel background + Zipf-ranked head) and parameters (T 0.7, top-p
 min-p 0.05, repetition 1.1, frequency 0.3, presence 0.2, 2,048-id histories), seeded per rank.
 A step is one ``lss_sample`` over the batch (K0 history pairs, K1 streaming pass, K2 per-row
 resolve, K3 dense rows), replayed as one CUDA graph; with N GPUs each rank samples its own 256
-rows (weak scaling) and the token ids are gathered to rank 0 with NCCL after each step.
+rows and keeps their tokens (weak scaling, no collective in the timed steps; the time is the
+maximum over ranks).  ``--workload`` selects another configuration: configs 1-4 in the same
+row mode (config 4 splits its 1,024 rows over the ranks), config 5 vocabulary-sharded (shard
+records, one all-gather, merge and draw on every rank).
 
 ``--impl reference`` times the reference's CPU implementation of the same path (the
 ``oracle.torch_port`` restatement of ``sample_next_token``, per-row loop, all host threads)
@@ -277,8 +280,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             _lib.check("lss_sample_rows", lib.lss_sample_rows(*args_, None, None, P(ws), ws.numel(), sp))
 
     def gather():
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, tokens)
+        # Rows are independent: every rank samples its own rows and keeps their tokens, so
+        # the timed steps take no collective (a deployment that wants the ids on one rank
+        # gathers them with RowShardSampler).
+        return
 
     def barrier():
         if world > 1:
@@ -383,10 +388,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                     for k in ("temperature", "top_k", "top_p", "min_p", "repetition_penalty",
                               "frequency_penalty", "presence_penalty")}
         dev_x = torch.empty_like(bufs[0])
-        tok_host = torch.empty(B * world, dtype=torch.int32).pin_memory()
+        tok_host = torch.empty(B, dtype=torch.int32).pin_memory()
         h2d = logits_host.numel() * logits_host.element_size() + host_u.numel() * 4 + host_off.numel() * 4 + \
             host_ids.numel() * 4 + sum(t.numel() * 4 for t in host_prm.values())
-        d2h = tok_host.numel() * 4 if rank == 0 else B * 4
+        d2h = B * 4
 
         def e2e_step():
             dev_x.copy_(logits_host, non_blocking=True)
@@ -396,11 +401,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             h_ids.copy_(host_ids, non_blocking=True)
             uni.copy_(host_u, non_blocking=True)
             s.sample(dev_x, prm, h_off, h_ids, uni, tokens_out=tokens)
-            if world > 1:
-                dist.all_gather_into_tensor(gathered, tokens)
-                tok_host.copy_(gathered, non_blocking=True)
-            else:
-                tok_host[:B].copy_(tokens, non_blocking=True)
+            tok_host[:B].copy_(tokens, non_blocking=True)  # each rank reads back its own rows
 
         for _ in range(2):
             e2e_step()
