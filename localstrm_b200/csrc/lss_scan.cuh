@@ -65,7 +65,7 @@ struct __align__(16) ScanCtl {
   ItemDesc desc[2 * SC_NST];   // by item (j % 4): a released stage's next item does not overwrite it
   ItemScratch sc[2];            // by item parity
   uint64_t best[2][32];         // greedy items: argmax code per warp
-  uint32_t wkey[2][32];         // sampled items: max key of z per warp (all ones: NaN / +inf)
+  uint32_t wkey[2][32];         // sampled items: [0] max key of z over the warps (all ones: NaN / +inf)
   uint32_t prm[SC_RING][12];    // T, k, min_p, rep, freq, pres, hist_off[row], segment bounds
 };
 
@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
   const int G = gridDim.x;
 
   if (tid < (int)(2 * sizeof(ItemScratch) / 4)) reinterpret_cast<uint32_t*>(ctl->sc)[tid] = 0u;  // cnt, flags
+  if (tid < 2) ctl->wkey[tid][0] = 0u;
   if (tid == 0) {
     for (int q = 0; q < SC_NST; ++q) {
       mbar_init(&ctl->full[q], 2);  // the logits' arrival, then the history pairs'
@@ -364,6 +365,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
       av = warp_allreduce(b, MaxU64());
     }
     if (lane == 0) {
+      ctl->wkey[ps][0] = 0u;  // every warp has read it (X of that item); ready for item + 2
       ItemScratch* q = &ctl->sc[ps];
       a.summ[(int64_t)prow * S + pslice] = make_uint4((uint32_t)av, (uint32_t)(av >> 32), q->cnt, q->flags);
       q->cnt = 0u;
@@ -413,7 +415,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
         tmax = fmax_nan(tmax, fmax_nan(fmax_nan(v[i].x, v[i].y), fmax_nan(v[i].z, v[i].w)));
       }
       const float wmax = warp_allreduce(tmax, MaxF());
-      if (lane == 0) ctl->wkey[ip][warp] = (!(wmax == wmax) || wmax == INFINITY) ? 0xffffffffu : f2key(wmax);
+      if (lane == 0) atomicMax(&ctl->wkey[ip][0], (!(wmax == wmax) || wmax == INFINITY) ? 0xffffffffu : f2key(wmax));
       if (k)
         for (int i = ctid; i < NBIN + 1; i += SC_CT) HL[i] = 0u;
     }
@@ -431,8 +433,7 @@ __global__ void __launch_bounds__(SC_NT, 1) lss_scan_kernel(const ScanArgs a) {
     // ---- X(j)
     uint32_t mk = 0;
     if (mode == ITEM_SAMPLE) {
-      mk = lane < SC_CW ? ctl->wkey[ip][lane] : 0u;
-      mk = warp_allreduce(mk, MaxU32());
+      mk = ctl->wkey[ip][0];
       const bool special = mk == 0xffffffffu;
       if (special && ctid == 0) atomicOr(&sc->flags, SUM_SPECIAL);
       const float M = key2f(mk);
