@@ -107,6 +107,56 @@ struct Row {
   }
 };
 
+// Scan of the NBIN bins of a merged histogram by one warp (every warp of the CTA computes the
+// same result): lane l holds bins 8l .. 8l+7 in ascending order, or bins NBIN-1-8l down to
+// NBIN-8-8l when `desc`.  Returns the first bin, in scan order, at which base plus the
+// inclusive cumulative measure exceeds `target` (reaches it when `ge`), with base plus the
+// measure of the bins scanned before it in `before`; -1 when no bin does.  `sum` gets base
+// plus the measure of all NBIN bins (the far bin NBIN is not included).
+__device__ __forceinline__ int warp_bin_cross(const uint32_t* hc, const uint64_t* hm, bool mass, bool desc,
+                                              uint64_t base, uint64_t target, bool ge, uint64_t& before,
+                                              uint64_t& sum) {
+  static_assert(NBIN == 256, "one warp scans 8 bins per lane");
+  const int lane = threadIdx.x & 31;
+  uint64_t c8[8];
+  uint64_t loc = 0;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int b = desc ? NBIN - 1 - (8 * lane + q) : 8 * lane + q;
+    c8[q] = mass ? hm[b] : (uint64_t)hc[b];
+    loc += c8[q];
+  }
+  uint64_t incl = loc;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint64_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  sum = base + __shfl_sync(0xffffffffu, incl, 31);
+  const unsigned hit = __ballot_sync(0xffffffffu, ge ? base + incl >= target : base + incl > target);
+  if (!hit) {
+    before = sum;
+    return -1;
+  }
+  const int L = __ffs(hit) - 1;
+  int qq = 7;
+  uint64_t run = base + incl - loc, bef = run;
+  bool seen = false;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const uint64_t nx = run + c8[q];
+    if (!seen && (ge ? nx >= target : nx > target)) {
+      seen = true;
+      qq = q;
+      bef = run;
+    }
+    run = nx;
+  }
+  const int r = __shfl_sync(0xffffffffu, 8 * lane + qq, L);
+  before = __shfl_sync(0xffffffffu, bef, L);
+  return desc ? NBIN - 1 - r : r;
+}
+
 // Result of a cluster-wide radix select.
 struct Sel {
   bool found;     // false when the whole measure is <= target (nothing to cut)
@@ -159,8 +209,9 @@ __device__ Sel radix_select(Row<CL>& R, uint32_t floorK, float m, uint64_t targe
   int p = R.template merge_hist<MASS>();
   const uint32_t* hc = R.mh_cnt + p * (NBIN + 1);
   const uint64_t* hm = R.mh_mass + p * (NBIN + 1);
-  uint64_t total = 0;
-  for (int b = 0; b <= NBIN; ++b) total += MASS ? hm[b] : (uint64_t)hc[b];
+  uint64_t acc, sum;
+  warp_bin_cross(hc, hm, MASS, false, 0, ~0ull, false, acc, sum);
+  const uint64_t total = sum + (MASS ? hm[NBIN] : (uint64_t)hc[NBIN]);
   s.total = total;
   uint64_t target = MASS ? (uint64_t)floor((double)total * (double)tp) : target_count;
   if (total <= target) {
@@ -169,12 +220,12 @@ __device__ Sel radix_select(Row<CL>& R, uint32_t floorK, float m, uint64_t targe
     R.zero_merged(p);
     return s;
   }
-  uint64_t acc = 0;
-  int b0 = NBIN;
-  for (int b = 0; b <= NBIN; ++b) {
-    uint64_t mb = MASS ? hm[b] : (uint64_t)hc[b];
-    if (acc + mb > target) { b0 = b; break; }
-    acc += mb;
+  // First bin (the far bin last) at which the cumulative measure exceeds the target; acc is
+  // the measure of the bins before it.
+  int b0 = warp_bin_cross(hc, hm, MASS, false, 0, target, false, acc, sum);
+  if (b0 < 0) {
+    b0 = NBIN;
+    acc = sum;
   }
   __syncthreads();
   R.zero_merged(p);
@@ -218,14 +269,9 @@ __device__ Sel radix_select(Row<CL>& R, uint32_t floorK, float m, uint64_t targe
     p = R.template merge_hist<MASS>();
     hc = R.mh_cnt + p * (NBIN + 1);
     hm = R.mh_mass + p * (NBIN + 1);
-    const int nb = (int)(range >> sh);  // highest bin index in use
-    int c = -1;
-    uint64_t a2 = A;
-    for (int bb = nb; bb >= 0; --bb) {
-      uint64_t mb = MASS ? hm[bb] : (uint64_t)hc[bb];
-      if (a2 + mb > target) { c = bb; break; }
-      a2 += mb;
-    }
+    // Highest bin first; the bins above (range >> sh) hold nothing.
+    uint64_t a2, s2;
+    const int c = warp_bin_cross(hc, hm, MASS, true, A, target, false, a2, s2);
     uint32_t cnt_c = c >= 0 ? hc[c] : 0;
     uint64_t mass_c = c >= 0 ? hm[c] : 0;
     __syncthreads();
@@ -452,50 +498,43 @@ __device__ void slow_row(Row<CL>& R, const RowArgs& a, const int row, uint32_t& 
     if (tid == 0) R.lh_cnt[NBIN] = far_c;
     const int hp = R.template merge_hist<false>();
     const uint32_t* hc = R.mh_cnt + hp * (NBIN + 1);
-    uint32_t acc = 0;
-    int b = 0;
-    for (; b < NBIN; ++b) {
-      acc += hc[b];
-      if (acc >= (uint32_t)k) break;
-    }
-    uint32_t total = acc;
-    if (b == NBIN) total += hc[NBIN];
-    if (b < NBIN) {
+    // First bin at which the cumulative count reaches k.
+    uint64_t before, sum;
+    const int b = warp_bin_cross(hc, R.mh_mass + hp * (NBIN + 1), false, false, 0, (uint64_t)k, true, before, sum);
+    if (b >= 0) {
       tk_bind = true;
       bk = b;
-    } else if (total > (uint32_t)k) {
+    } else if (sum + hc[NBIN] > (uint64_t)k) {
       need_dense = true;  // the k-th largest is more than 16 nats below the max
     }
     __syncthreads();
     R.zero_merged(hp);
   }
 
-  // ---- compaction of the window into a local list
+  // ---- compaction of the window into a local list: every thread counts what it keeps, a
+  // block scan places the threads' runs, and the list is written only when it fits (a CTA
+  // over LCAP sends the row to the dense path, which needs no list).
   if (!need_dense) {
-    if (tid == 0) ctl->lcount = 0;
-    __syncthreads();
-    const int lane = tid & 31;
-    for (int q = tid; q - lane < n4; q += NT) {  // warp-uniform trip count
-      float4 v = q < n4 ? t4[q] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      float ys[4] = {v.x, v.y, v.z, v.w};
+    auto keep = [&](float y) {
+      return f2key(y) >= Kmp && y > -INFINITY && (!tk_bind || vbin(y, m) <= bk);
+    };
+    uint32_t mine = 0;
+    for (int q = tid; q < n4; q += NT) {
+      const float4 v = t4[q];
+      mine += (uint32_t)keep(v.x) + (uint32_t)keep(v.y) + (uint32_t)keep(v.z) + (uint32_t)keep(v.w);
+    }
+    uint32_t ctot;
+    uint32_t pos = block_excl_scan(mine, ctl->r32, ctot);
+    if (ctot <= (uint32_t)SM::LCAP) {
+      for (int q = tid; q < n4; q += NT) {
+        const float4 v = t4[q];
+        const float ys[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t key = f2key(ys[j]);
-        bool keep = key >= Kmp && ys[j] > -INFINITY && (!tk_bind || vbin(ys[j], m) <= bk);
-        const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-        if (bal) {
-          uint32_t base = 0;
-          const int leader = __ffs(bal) - 1;
-          if (lane == leader) base = atomicAdd(&ctl->lcount, (uint32_t)__popc(bal));
-          base = __shfl_sync(0xffffffffu, base, leader);
-          if (keep) {
-            const uint32_t pos = base + __popc(bal & ((1u << lane) - 1u));
-            if (pos < (uint32_t)SM::LCAP)
-              R.lcand[pos] = ((uint64_t)key << 32) | (uint32_t)(~(uint32_t)(lo + 4 * q + j));
-          }
-        }
+        for (int j = 0; j < 4; ++j)
+          if (keep(ys[j])) R.lcand[pos++] = ((uint64_t)f2key(ys[j]) << 32) | (uint32_t)(~(uint32_t)(lo + 4 * q + j));
       }
     }
+    if (tid == 0) ctl->lcount = ctot;
     __syncthreads();
   }
   const uint32_t lcount = need_dense ? 0xffffffffu : ctl->lcount;
