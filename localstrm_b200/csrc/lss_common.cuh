@@ -249,9 +249,35 @@ struct SumD { __device__ double operator()(double a, double b) const { return a 
 struct MinI { __device__ int operator()(int a, int b) const { return a < b ? a : b; } };
 
 // Bitonic sort of a[0, np) (np a power of two) in shared memory, whole CTA.
+// Steps whose partner distance j is below 32 pair elements inside aligned runs of 32: each
+// warp takes such runs, one element per lane, and does those steps with shuffles, so only
+// the steps with j >= 32 go through shared memory with a block barrier each (28 barriers
+// instead of 66 for np = 2048).
 __device__ __forceinline__ void bitonic_sort(uint64_t* a, int np, bool descending) {
-  for (int k = 2; k <= np; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
+  const int lane = threadIdx.x & 31;
+  // Levels k_first .. k_last on every run of 32, the last one from step jmax_last down
+  // (lanes past np hold placeholders and pair only with each other, np being a power of two).
+  auto runs = [&](int k_first, int k_last, int jmax_last) {
+    for (int base = (threadIdx.x >> 5) * 32; base < np; base += NT) {
+      const int i = base + lane;
+      uint64_t v = i < np ? a[i] : 0ull;
+      for (int k = k_first; k <= k_last; k <<= 1) {
+        for (int j = k == k_last ? jmax_last : k >> 1; j > 0; j >>= 1) {
+          const uint64_t o = __shfl_xor_sync(0xffffffffu, v, j);
+          const bool asc = ((i & k) == 0) != descending;
+          const bool keep_small = ((i & j) == 0) == asc;
+          v = keep_small ? (o < v ? o : v) : (o > v ? o : v);
+        }
+      }
+      if (i < np) a[i] = v;
+    }
+    __syncthreads();
+  };
+  if (np < 2) return;
+  const int k0 = np < 32 ? np : 32;
+  runs(2, k0, k0 >> 1);  // levels 2 .. 32 entirely inside the runs
+  for (int k = 64; k <= np; k <<= 1) {
+    for (int j = k >> 1; j >= 32; j >>= 1) {
       for (int i = threadIdx.x; i < np; i += NT) {
         int p = i ^ j;
         if (p > i) {
@@ -265,6 +291,7 @@ __device__ __forceinline__ void bitonic_sort(uint64_t* a, int np, bool descendin
       }
       __syncthreads();
     }
+    runs(k, k, 16);
   }
 }
 // Bitonic sort of one u64 per lane across a warp (descending when `descending`).
