@@ -22,6 +22,7 @@
 namespace lss {
 
 constexpr int SHARD_CAND = 2048;   // candidates one shard CTA sorts
+constexpr int SH_U = 8;            // loads in flight per thread in the shard passes
 constexpr int MERGE_CAP = 2048;    // shards x K codes the merge CTA holds
 constexpr uint32_t SHARD_OVER = 1u;     // more values at the floor than SHARD_CAND
 constexpr uint32_t SHARD_SPECIAL = 2u;  // NaN / +inf in the shard
@@ -53,14 +54,31 @@ __global__ void __launch_bounds__(NT) lss_shard_kernel(const void* logits, int64
   const float T = temperature[row];
   const bool greedy = T <= 0.0f;  // codes of the raw values (their order is all a greedy row needs)
   auto y_of = [&](float z) -> float { return greedy ? z : __fdiv_rn(z, T); };
+  // Each pass loads SH_U values per thread (elements i0 + u * NT) before it works on them, so
+  // that SH_U loads per thread are in flight; a thread sees its elements in the same order as
+  // with one load per step.
+  auto load_batch = [&](int i0, float (&zb)[SH_U]) {
+#pragma unroll
+    for (int u = 0; u < SH_U; ++u) {
+      const int i = i0 + u * NT;
+      zb[u] = i < Vs ? z_at(i) : -INFINITY;
+    }
+  };
   // ---- pass 1: the shard max of y (y is monotone in z for T > 0) and its argmax, NaN first
   float zm = -INFINITY;
   uint64_t best = 0;
-  for (int i = tid; i < Vs; i += NT) {
-    const float z = z_at(i);
-    zm = fmax_nan(zm, z);
-    const uint64_t c = argmax_code(z, i);
-    best = c > best ? c : best;
+  for (int i0 = tid; i0 < Vs; i0 += SH_U * NT) {
+    float zb[SH_U];
+    load_batch(i0, zb);
+#pragma unroll
+    for (int u = 0; u < SH_U; ++u) {
+      const int i = i0 + u * NT;
+      if (i < Vs) {
+        zm = fmax_nan(zm, zb[u]);
+        const uint64_t c = argmax_code(zb[u], i);
+        best = c > best ? c : best;
+      }
+    }
   }
   zm = block_allreduce(zm, MaxF(), rf);
   best = block_allreduce(best, MaxU64(), r64);
@@ -97,12 +115,18 @@ __global__ void __launch_bounds__(NT) lss_shard_kernel(const void* logits, int64
     __syncthreads();
     const float bs = __fdiv_rn(1.0f, bw);
     double sl = 0.0;
-    for (int i = tid; i < Vs; i += NT) {
-      const float y = y_of(z_at(i));
-      if (y == -INFINITY) continue;
-      if (scale == 0) sl += (double)expf(__fsub_rn(y, my));
-      const float d = __fmul_rn(__fsub_rn(my, y), bs);
-      atomicAdd(&HLw[warp][d < (float)NBIN ? (int)d : NBIN], 1u);
+    for (int i0 = tid; i0 < Vs; i0 += SH_U * NT) {
+      float zb[SH_U];
+      load_batch(i0, zb);
+#pragma unroll
+      for (int u = 0; u < SH_U; ++u) {
+        if (i0 + u * NT >= Vs) continue;
+        const float y = y_of(zb[u]);
+        if (y == -INFINITY) continue;
+        if (scale == 0) sl += (double)expf(__fsub_rn(y, my));
+        const float d = __fmul_rn(__fsub_rn(my, y), bs);
+        atomicAdd(&HLw[warp][d < (float)NBIN ? (int)d : NBIN], 1u);
+      }
     }
     if (scale == 0) se = block_allreduce(sl, SumD(), rd);
     __syncthreads();
@@ -159,23 +183,28 @@ __global__ void __launch_bounds__(NT) lss_shard_kernel(const void* logits, int64
   }
   if (tid == 0) s_n = 0u;
   __syncthreads();
-  for (int i0 = 0; i0 < Vs; i0 += NT) {  // uniform trip count
-    const int i = i0 + tid;
-    bool keep = false;
-    uint64_t code = 0;
-    if (i < Vs) {
-      const float y = y_of(z_at(i));
-      keep = y > -INFINITY && y >= ythr;
-      code = ((uint64_t)f2key(y) << 32) | (uint32_t)(~(uint32_t)(voff + i));
-    }
-    const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-    if (bal) {
-      const int leader = __ffs(bal) - 1;
-      uint32_t base = 0;
-      if (lane == leader) base = atomicAdd(&s_n, (uint32_t)__popc(bal));
-      base = __shfl_sync(0xffffffffu, base, leader);
-      const uint32_t pos = base + __popc(bal & ((1u << lane) - 1u));
-      if (keep && pos < (uint32_t)SHARD_CAND) C[pos] = code;
+  for (int j0 = 0; j0 < Vs; j0 += SH_U * NT) {  // uniform trip count
+    float zb[SH_U];
+    load_batch(j0 + tid, zb);
+#pragma unroll
+    for (int u = 0; u < SH_U; ++u) {
+      const int i = j0 + u * NT + tid;
+      bool keep = false;
+      uint64_t code = 0;
+      if (i < Vs) {
+        const float y = y_of(zb[u]);
+        keep = y > -INFINITY && y >= ythr;
+        code = ((uint64_t)f2key(y) << 32) | (uint32_t)(~(uint32_t)(voff + i));
+      }
+      const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+      if (bal) {
+        const int leader = __ffs(bal) - 1;
+        uint32_t base = 0;
+        if (lane == leader) base = atomicAdd(&s_n, (uint32_t)__popc(bal));
+        base = __shfl_sync(0xffffffffu, base, leader);
+        const uint32_t pos = base + __popc(bal & ((1u << lane) - 1u));
+        if (keep && pos < (uint32_t)SHARD_CAND) C[pos] = code;
+      }
     }
   }
   __syncthreads();
