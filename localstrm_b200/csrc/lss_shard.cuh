@@ -22,7 +22,7 @@
 namespace lss {
 
 constexpr int SHARD_CAND = 2048;   // candidates one shard CTA sorts
-constexpr int SH_U = 8;            // loads in flight per thread in the shard passes
+constexpr int SH_U = 12;           // loads in flight per thread in the shard passes
 constexpr int MERGE_CAP = 2048;    // shards x K codes the merge CTA holds
 constexpr uint32_t SHARD_OVER = 1u;     // more values at the floor than SHARD_CAND
 constexpr uint32_t SHARD_SPECIAL = 2u;  // NaN / +inf in the shard
