@@ -4,15 +4,17 @@ Workload (the metric point): B=256 rows per GPU, V=151,936, float32 logits with 
 distribution (Gumbel background + Zipf-ranked head) and parameters (T 0.7, top-p 0.95,
 min-p 0.05, repetition 1.1, frequency 0.3, presence 0.2, 2,048-id histories), seeded per rank.
 A step is one ``lss_sample`` over the batch (K0 history pairs, K1 streaming pass, K2 per-row
-resolve, K3 dense rows), replayed as one CUDA graph; with N GPUs each rank samples its own 256
-rows and keeps their tokens (weak scaling, no collective in the timed steps; the time is the
-maximum over ranks).  ``--workload`` selects another configuration: configs 1-4 in the same
-row mode (config 4 splits its 1,024 rows over the ranks), config 5 vocabulary-sharded (shard
-records, one all-gather, merge and draw on every rank).
+resolve, K3 dense rows), replayed as one CUDA graph.  With N GPUs (one process per GPU) each
+rank samples its own rows and every step ends with the row mode's exchange, one NCCL
+all-gather of the int32 token ids, inside the timed region; the time is the maximum over
+ranks.  By default every rank has its own 256 rows (weak scaling); ``--strong`` splits the
+one 256-row batch over the ranks instead.  ``--workload`` selects another configuration:
+configs 1-4 in the same row mode (config 4 always splits its 1,024 rows over the ranks),
+config 5 vocabulary-sharded (shard records, one all-gather, merge and draw on every rank).
 
 ``--impl reference`` times the reference's CPU implementation of the same path (the
 ``oracle.torch_port`` restatement of ``sample_next_token``, per-row loop, all host threads)
-on a bounded sample of the same rows.
+on a bounded sample of the same rows per step, and reports the measured time of those steps.
 
 Prints one JSON line on rank 0.
 """
@@ -194,12 +196,21 @@ def _row_block(w, start: int, stop: int):
     return b
 
 
-def make_workload(rank: int, world: int = 1, name: str = "headline"):
-    """The rank's rows of a row-mode workload; config 4's 1,024 rows are split over the ranks
-    (strong scaling), every other workload gives each rank its own batch (weak scaling)."""
+def is_strong(args) -> bool:
+    return args.workload == "cfg4" or (args.workload == "headline" and args.strong)
+
+
+def make_workload(rank: int, world: int = 1, name: str = "headline", strong: bool = False):
+    """The rank's rows of a row-mode workload; config 4's 1,024 rows (and with ``strong`` the
+    headline's 256) are split over the ranks (strong scaling), every other workload gives each
+    rank its own batch (weak scaling)."""
     from localstrm_b200 import workloads as wl
     from localstrm_b200.distributed import shard_rows
     if name == "headline":
+        if strong:
+            full = wl.headline(seed=0, B=B_PER_GPU, V=V)
+            a, b = shard_rows(full.B, world, rank)
+            return _row_block(full, a, b)
         return wl.headline(seed=rank, B=B_PER_GPU, V=V)
     if name == "cfg4":
         full = wl.config4(seed=0)
@@ -208,29 +219,75 @@ def make_workload(rank: int, world: int = 1, name: str = "headline"):
     return {"cfg1": wl.config1, "cfg2": wl.config2, "cfg3": wl.config3}[name](seed=rank)
 
 
+def row_config(args, w, world: int) -> dict:
+    """The ``config`` of a row-mode line (both arms print the same one)."""
+    esize = 4 if w.dtype == "f32" else 2
+    buf = w.B * w.V * esize
+    desc = DESC[args.workload]
+    if is_strong(args) and args.workload == "headline":
+        desc = desc.replace("B=256 rows/GPU", "B=256 rows split over the GPUs")
+    return {"workload": desc,
+            "global_batch": w.B * world if not is_strong(args) else
+            {"cfg4": 1024, "headline": B_PER_GPU}[args.workload],
+            "rows_per_gpu": w.B, "vocab": w.V,
+            "parallelism": f"rows{world}" if world > 1 else "single",
+            "l2": f"{n_buffers(buf)} rotating input buffers of {buf / 1e6:.1f} MB (together > 2 x 126 MB L2)",
+            "inner_reps": max(1, args.inner)}
+
+
+def vocab_config(args, w, world: int) -> dict:
+    from localstrm_b200.distributed import shard_vocab
+    off, end = shard_vocab(w.V, world, 0)
+    buf = w.B * (end - off) * 4
+    return {"workload": DESC["cfg5"], "global_batch": w.B, "vocab": w.V, "vocab_per_gpu": end - off,
+            "parallelism": f"vocab{world}",
+            "l2": f"{n_buffers(buf)} rotating shard buffers of {buf / 1e6:.1f} MB (together > 2 x 126 MB L2)"}
+
+
 def run_reference(args, rank: int, world: int):
+    """The reference's per-row CPU path on rank 0's rows: each step samples a bounded number
+    of rows (sized from the warm-up so that the timed steps take about ``--ref-seconds``);
+    ``ms_per_step`` is the measured time of those steps."""
     if rank != 0:
         return
-    w = make_workload(0, 1, args.workload) if args.workload != "cfg5" else _cfg5_full()
-    rates = []
-    meta = None
-    for i in range(args.warmup + args.steps):
-        rate, cores, n, dt = cpu_reference_rate(w, seconds=args.cpu_seconds / max(args.steps, 1),
-                                                min_rows=4)
-        if i >= args.warmup:
-            rates.append(rate)
-            meta = (cores, n, dt)
-    value = statistics.median(rates)
-    cores, n, dt = meta
+    from oracle import torch_port as TP
+    if args.workload == "cfg5":
+        w = _cfg5_full()
+        config = vocab_config(args, w, world)
+    else:
+        w = make_workload(0, world, args.workload, is_strong(args))
+        config = row_config(args, w, world)
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    gen = torch.Generator().manual_seed(0)
+    nxt = 0
+
+    def sample(n):
+        nonlocal nxt
+        t0 = time.perf_counter()
+        for _ in range(n):
+            TP.sample_workload_rows(w, [nxt % w.B], gen)
+            nxt += 1
+        return time.perf_counter() - t0
+
+    per_row = []
+    for _ in range(args.warmup):
+        per_row.append(sample(2) / 2)
+    t_row = statistics.median(per_row)
+    rows_per_step = int(max(1, min(w.B, round(args.ref_seconds / max(args.steps, 1) / t_row))))
+    step_s = [sample(rows_per_step) for _ in range(args.steps)]
+    total = sum(step_s)
+    value = rows_per_step * args.steps / total
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * w.B / value, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": w.dtype, "data": "synthetic (seeded)",
-        "config": {"workload": DESC[args.workload], "global_batch": w.B, "parallelism": "cpu"},
+        "ms_per_step": 1000.0 * total / args.steps, "higher_is_better": True,
+        "scaling": "strong" if (is_strong(args) or args.workload == "cfg5") else "weak",
+        "vs_baseline": None, "dtype": w.dtype, "data": "synthetic (seeded)", "config": config,
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": cores, "kind": "port",
-                         "sample": f"{n} rows of the workload per step (~{dt:.1f} s), per-row "
-                                   "sample_next_token restated in torch CPU ops"},
+                         "sample": f"{rows_per_step} rows of rank 0's batch per step ({args.steps} steps, "
+                                   f"{total:.1f} s): per-row sample_next_token restated in torch CPU ops "
+                                   "(oracle/torch_port.py), all host threads"},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -244,7 +301,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     lib = _lib.load()
-    w = make_workload(rank, world, args.workload)
+    w = make_workload(rank, world, args.workload, is_strong(args))
     B = w.B
     DTC = DT_CODE[w.dtype]
     logits_host = torch.from_numpy(w.logits).to(TORCH_DT[w.dtype]).pin_memory()
@@ -280,10 +337,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             _lib.check("lss_sample_rows", lib.lss_sample_rows(*args_, None, None, P(ws), ws.numel(), sp))
 
     def gather():
-        # Rows are independent: every rank samples its own rows and keeps their tokens, so
-        # the timed steps take no collective (a deployment that wants the ids on one rank
-        # gathers them with RowShardSampler).
-        return
+        # The row mode's exchange step (RowShardSampler): every rank's token ids to every
+        # rank, one NCCL all-gather of B int32 per rank on the step's stream.
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, tokens)
 
     def barrier():
         if world > 1:
@@ -432,21 +489,17 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     paths = s.row_paths(B)
     flags = s.status()
-    global_b = B * world
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "strong" if args.workload == "cfg4" else "weak",
+            "higher_is_better": True, "scaling": "strong" if is_strong(args) else "weak",
             "vs_baseline": None, "dtype": w.dtype,
             "data": "synthetic (seeded; " + ("config 3 distribution at V=151,936)" if args.workload == "headline"
                                              else f"{args.workload})"),
-            "config": {"workload": DESC[args.workload],
-                       "global_batch": global_b, "rows_per_gpu": B, "vocab": w.V,
-                       "parallelism": f"rows{world}" if world > 1 else "single",
-                       "l2": f"{NBUF} rotating input buffers of {logits_host.numel() * logits_host.element_size() / 1e6:.1f} MB"
-                             f" (together > 2 x 126 MB L2)",
-                       "inner_reps": reps},
+            "config": row_config(args, w, world),
+            "exchange": "NCCL all-gather of the token ids after every step, inside the timed region"
+                        if world > 1 else None,
             "hbm_gbs": alg * world * n_steps_total / (elapsed_ms / 1000.0) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
@@ -553,10 +606,7 @@ def run_vocab(args, rank: int, world: int, local_rank: int):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded; cfg5)",
-            "config": {"workload": DESC["cfg5"], "global_batch": B, "vocab": Vt, "vocab_per_gpu": Vs,
-                       "parallelism": f"vocab{world}", "records_bytes_per_rank": B * rb,
-                       "l2": f"{nbuf} rotating shard buffers of {shard_host.numel() * 4 / 1e6:.1f} MB"
-                             f" (together > 2 x 126 MB L2)"},
+            "config": vocab_config(args, w, world), "records_bytes_per_rank": B * rb,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None, "kernel": "lss_shard_kernel",
                          "peak_source": peak_kind, "algorithmic_bytes_per_launch": alg, "kernel_ms": kern_ms},
@@ -576,6 +626,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--workload", default="headline", choices=WORKLOADS,
                     help="headline (the metric point) or one of the other configurations")
+    ap.add_argument("--strong", action="store_true",
+                    help="headline: split one 256-row batch over the GPUs instead of 256 rows per GPU")
+    ap.add_argument("--ref-seconds", type=float, default=40.0,
+                    help="--impl reference: CPU time of the timed steps together")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -24,8 +24,10 @@
  *    greedy on the raw logits (penalties ignored); top_k <= 0 disables top-k;
  *    top_p outside (0,1) disables top-p; min_p outside (0,1) disables min-p;
  *    repetition_penalty == 1 and frequency == presence == 0 disable penalties.
- *  - Histories are CSR: hist_offsets[B+1] (int32, device) into hist_ids (int32,
- *    device, values in [0, V)).  hist_offsets may be NULL when hist_total == 0.
+ *  - Histories are CSR: hist_offsets[B+1] (int32, device, non-decreasing, within
+ *    [0, hist_total]) into hist_ids (int32, device, hist_total values in [0, V)).
+ *    hist_offsets may be NULL when hist_total == 0.  The kernels check every row's offsets
+ *    and ids and raise LSS_FLAG_BAD_HISTORY instead of reading outside the arrays.
  *  - uniforms[B] (device, f32 in [0,1)) drive the draw: the token is the first
  *    vocabulary index whose running probability mass exceeds u * total, over the
  *    kept tokens in index order (inverse CDF).  The reference uses
@@ -55,7 +57,11 @@ extern "C" {
 
 /* Device-side error flags (lss_read_status). */
 #define LSS_FLAG_TMA_TIMEOUT 0x1u     /* a bounded wait for a bulk copy gave up */
-#define LSS_FLAG_BAD_HISTORY 0x2u     /* a history id outside [0, V) was ignored */
+#define LSS_FLAG_BAD_HISTORY 0x2u     /* a history id outside [0, V) was ignored, or a row's CSR
+                                         offsets lay outside [0, hist_total] or decreased (that
+                                         row's history was ignored; rows whose ranges overlap
+                                         give unreliable tokens, but nothing is read or written
+                                         out of bounds) */
 #define LSS_FLAG_INTERNAL 0x4u        /* an internal capacity check failed (result unreliable) */
 
 /* Per-row path codes written to the workspace (lss_read_row_paths). */
@@ -170,7 +176,10 @@ int lss_argmax(const void* logits, int dtype, int B, int V, int64_t row_stride,
  * make that first call before any stream capture.  All calls on a device share the one
  * array: two calls that overlap on the GPU (different streams, no ordering between them)
  * race on it and give wrong tokens; serialise them.  Everything that must start at zero
- * is cleared by the call itself.  lss_read_status / lss_read_row_paths do not apply. */
+ * is cleared by the call itself.  The looked-up address is kept for the life of the process:
+ * after cudaDeviceReset on a device (which unloads this library's device code there) do not
+ * call lss_sample_noalloc on that device again.  lss_read_status / lss_read_row_paths take a
+ * caller workspace and do not apply; lss_noalloc_read_status reads this call's flags. */
 #define LSS_NOALLOC_SCRATCH_BYTES (32u << 20)
 int lss_sample_noalloc(const void* logits, int dtype, int B, int V, int64_t row_stride,
                        const float* temperature, const int32_t* top_k, const float* top_p,
@@ -179,6 +188,12 @@ int lss_sample_noalloc(const void* logits, int dtype, int B, int V, int64_t row_
                        const int32_t* hist_offsets, const int32_t* hist_ids,
                        int64_t hist_total, const float* uniforms, int32_t* tokens_out,
                        uint8_t* kept_out, float* probs_out, void* stream);
+
+/* Device error flags (LSS_FLAG_*) of the last lss_sample_noalloc call on the current device:
+ * synchronises `stream`, then reads the status word of the fixed scratch, as lss_read_status
+ * does for a caller workspace.  LSS_ERR_DEVICE when a flag is set (the tokens of that call are
+ * then unreliable), LSS_OK otherwise.  No counterpart in the reference.  Allocates nothing. */
+int lss_noalloc_read_status(uint32_t* flags_out, void* stream);
 
 /* Token-id part of check_stop_criteria (sampling.py:166-196), batched and on the device, so
  * that a decode loop learns which rows stopped without reading every token back:

@@ -55,6 +55,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.lss_shard_topk.argtypes = [P, c_int, c_int, c_int, c_int64, c_int64, P, c_int, P, P]
     lib.lss_shard_merge.restype = c_int
     lib.lss_shard_merge.argtypes = [P, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, c_size_t, P]
+    lib.lss_noalloc_read_status.restype = c_int
+    lib.lss_noalloc_read_status.argtypes = [P, P]
     lib.lss_sample_noalloc.restype = c_int
     lib.lss_sample_noalloc.argtypes = [P, c_int, c_int, c_int, c_int64, P, P, P, P, P, P, P, P, P,
                                        c_int64, P, P, P, P, P]

@@ -359,6 +359,17 @@ __device__ __forceinline__ float z_floor_for(float y_thr, float T) {
   return __double2float_rd(z - slack);
 }
 
+// History range [b, e) of a row from the caller's CSR offsets.  Offsets outside [0, H] or
+// decreasing ones give an empty range and false (the caller raises LSS_FLAG_BAD_HISTORY), so
+// that no kernel reads or writes outside the id arrays and the workspace regions sized by H.
+__device__ __forceinline__ bool hist_range(const int32_t* off, int row, int H, int& b, int& e) {
+  const int b0 = off[row], e0 = off[row + 1];
+  const bool ok = 0 <= b0 && b0 <= e0 && e0 <= H;
+  b = ok ? b0 : 0;
+  e = ok ? e0 : 0;
+  return ok;
+}
+
 // ---------------------------------------------------------------------------
 // Arguments of the per-row kernels
 // ---------------------------------------------------------------------------
@@ -368,6 +379,7 @@ struct RowArgs {
   int B, V, TE;        // TE: tile elements per CTA (multiple of 16)
   int tile_bytes;      // bytes reserved for the tile
   int use_hist;
+  int H;                     // total history ids (hist_total)
   const float* temperature;
   const int32_t* top_k;
   const float* top_p;
@@ -397,7 +409,8 @@ struct RowArgs {
 // kernel's per-slice (id, count) segment, entries [first, last).
 __device__ __forceinline__ void apply_patches_global(const RowArgs& a, int row, int me, int lo, int n,
                                                      float* tile, int first) {
-  const int base = a.hist_off[row];
+  int base = 0, hend = 0;
+  hist_range(a.hist_off, row, a.H, base, hend);
   const int* so = a.seg_off + (int64_t)row * (MAXCL + 1);
   const int s0 = so[me], s1 = so[me + 1];
   const float rp = a.rep[row], fq = a.freq[row], pr = a.pres[row];

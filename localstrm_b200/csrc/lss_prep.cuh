@@ -36,7 +36,8 @@ __device__ void prep_row(const RowArgs& a, int row, bool active, int TE, int nse
     if (tid <= nseg) o.so[tid] = 0;
     return;
   }
-  const int b = a.hist_off[row], e = a.hist_off[row + 1];
+  int b = 0, e = 0;
+  if (!hist_range(a.hist_off, row, a.H, b, e)) atomicOr(o.bad, LSS_FLAG_BAD_HISTORY);
   const int H = e - b;
   if (H <= 0) {
     if (tid <= nseg) o.so[tid] = 0;
@@ -195,16 +196,15 @@ __global__ void __launch_bounds__(HIST_NT) lss_hist_kernel(const HistArgs h) {
   const float mp = a.min_p[row];
   const float rp = a.rep[row], fq = a.freq[row], pr = a.pres[row];
   int b = 0, e = 0;
-  if (a.use_hist) {
-    b = a.hist_off[row];
-    e = a.hist_off[row + 1];
-  }
+  bool bad_range = false;
+  if (a.use_hist) bad_range = !hist_range(a.hist_off, row, a.H, b, e);
   const bool bounded = (k > 0 && k < a.V) || (mp > 0.0f && mp < 1.0f) || a.V <= FAST_CAP / 2;
   const bool active = a.use_hist && T > 0.0f && bounded && (rp != 1.0f || fq != 0.0f || pr != 0.0f);
   const int nseg = h.S;
   int32_t* so = h.seg2 + (int64_t)row * (nseg + 1);
   const PrepOut o{so, h.rowflag + row};
   const int H = active ? e - b : 0;
+  if (bad_range && tid == 0) atomicOr(o.bad, LSS_FLAG_BAD_HISTORY);  // thread 0 cleared it above
   if (!active || H <= 0) {
     if (tid <= nseg) so[tid] = 0;
     return;

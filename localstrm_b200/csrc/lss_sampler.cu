@@ -425,6 +425,7 @@ int lss_sample_prepare(int B, int V, const float* temperature, const int32_t* to
   h.r.B = B;
   h.r.V = V;
   h.r.use_hist = hist_total > 0 ? 1 : 0;
+  h.r.H = (int)hist_total;
   h.r.temperature = temperature;
   h.r.top_k = top_k;
   h.r.min_p = min_p;
@@ -507,6 +508,7 @@ static int sample_rows(const void* logits, int dtype, int B, int V, int64_t row_
   a.TE = pl.TE;
   a.tile_bytes = pl.slow_tile;
   a.use_hist = hist_total > 0 ? 1 : 0;
+  a.H = (int)hist_total;
   a.temperature = temperature;
   a.top_k = top_k;
   a.top_p = top_p;
@@ -643,6 +645,14 @@ int lss_sample_noalloc(const void* logits, int dtype, int B, int V, int64_t row_
   return lss_sample(logits, dtype, B, V, row_stride, temperature, top_k, top_p, min_p, repetition_penalty,
                     frequency_penalty, presence_penalty, hist_offsets, hist_ids, hist_total, uniforms,
                     tokens_out, kept_out, probs_out, ws, (size_t)LSS_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+int lss_noalloc_read_status(uint32_t* flags_out, void* stream) {
+  if (!flags_out) return LSS_ERR_INVALID_ARG;
+  void* ws = nullptr;
+  int rc = lss::noalloc_scratch(&ws);
+  if (rc != LSS_OK) return rc;
+  return lss_read_status(ws, flags_out, stream);
 }
 
 size_t lss_shard_record_bytes(int K) { return K < 1 ? 0 : shard_record_bytes(K); }

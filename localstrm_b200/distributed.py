@@ -127,8 +127,37 @@ class VocabShardSampler:
             probs.data_ptr() if probs is not None else None, self._ws.data_ptr(), self._ws.numel(), stream))
         return tokens
 
+    def check_params(self, top_k=None, min_p=None, repetition_penalty=None, frequency_penalty=None,
+                     presence_penalty=None) -> None:
+        """Raises ``ValueError`` unless every row's reference parameters mean what this mode
+        computes: top-k with ``k = K``, no min-p and no penalties (``sampling.py:38-115``).
+        Arguments are the rows' values (sequences or tensors; ``None`` skips a field)."""
+        def vals(x):
+            if x is None:
+                return None
+            return (x.detach().cpu().tolist() if isinstance(x, torch.Tensor) else list(x))
+        k = vals(top_k)
+        if k is not None and any(int(v) != self.K for v in k):
+            raise ValueError(f"vocabulary-sharded mode applies top-k with k={self.K}; rows with another "
+                             "top_k (or top-k disabled) must be sampled in row mode")
+        mp = vals(min_p)
+        if mp is not None and any(0.0 < float(v) < 1.0 for v in mp):
+            raise ValueError("vocabulary-sharded mode does not apply min-p; sample such rows in row mode")
+        for name, x, neutral in (("repetition_penalty", repetition_penalty, 1.0),
+                                 ("frequency_penalty", frequency_penalty, 0.0),
+                                 ("presence_penalty", presence_penalty, 0.0)):
+            v = vals(x)
+            if v is not None and any(float(e) != neutral for e in v):
+                raise ValueError(f"vocabulary-sharded mode does not apply {name}; sample such rows in row mode")
+
     # ---- the step
-    def sample(self, logits, offset: int, V_total: int, temperature, top_p, uniforms) -> torch.Tensor:
+    def sample(self, logits, offset: int, V_total: int, temperature, top_p, uniforms,
+               **row_params) -> torch.Tensor:
+        """One token per row.  ``row_params`` (``top_k``, ``min_p``, ``repetition_penalty``,
+        ``frequency_penalty``, ``presence_penalty``) are checked with ``check_params`` first
+        when given."""
+        if row_params:
+            self.check_params(**row_params)
         world, _ = _world(self.group)
         B = logits.shape[0]
         rec = self._records(logits, offset, temperature, self.K)

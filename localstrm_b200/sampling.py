@@ -169,8 +169,13 @@ class BatchSampler:
         hist_total = 0
         if hist_ids is not None and hist_ids.numel() > 0:
             hist_total = int(hist_ids.numel())
-            if hist_offsets is None or hist_offsets.numel() != B + 1:
-                raise ValueError(f"hist_offsets: expected int32 [{B + 1}]")
+            # The library reads these as int32 device arrays: an int64 CSR would be read as
+            # pairs of int32 words.  Offsets' values are checked on the device (a bad row sets
+            # LSS_FLAG_BAD_HISTORY and its history is ignored).
+            for name, t, n in (("hist_offsets", hist_offsets, B + 1), ("hist_ids", hist_ids, hist_total)):
+                if t is None or t.dtype != torch.int32 or t.numel() != n or t.device != self.device \
+                        or not t.is_contiguous():
+                    raise ValueError(f"{name}: expected a contiguous int32 tensor of {n} entries on {self.device}")
         if tokens_out is None:
             tokens_out = torch.empty(B, dtype=torch.int32, device=self.device)
         ws = self.workspace(B, V, hist_total)

@@ -107,3 +107,33 @@ def test_noalloc_rejects_requests_beyond_its_fixed_scratch():
     assert "scratch" in _lib.status_string(6)
     assert lib.lss_workspace_bytes(256, V, 256 * 2048) <= limit   # the headline fits
     assert lib.lss_sample_noalloc(*([1, 0, 0, V, V] + [1] * 7 + [1, 1, 0, 1, 1, None, None, None])) == 0
+
+
+def test_history_csr_dtype_and_shape_are_checked_on_the_host():
+    """An int64 CSR (torch's default for Python ints) or a wrong-sized one is refused before
+    anything reaches the library, which reads int32 arrays."""
+    import torch
+    s = S.BatchSampler.__new__(S.BatchSampler)  # no device needed: the checks run first
+    s.device = torch.device("cpu")
+    s.lib = _lib.load()
+    s._ws = None
+    s._ws_bytes = 0
+    s._last_ws = None
+    B, V = 2, 16
+    x = torch.zeros(B, V)
+    prm = S.RowParams.from_arrays("cpu", temperature=[1, 1], top_k=[5, 5], top_p=[1, 1], min_p=[0, 0],
+                                  repetition_penalty=[1.1, 1.1], frequency_penalty=[0, 0],
+                                  presence_penalty=[0, 0])
+    u = torch.zeros(B)
+    good_off = torch.tensor([0, 2, 3], dtype=torch.int32)
+    good_ids = torch.tensor([1, 2, 3], dtype=torch.int32)
+    for off, ids in ((good_off.long(), good_ids), (good_off, good_ids.long()),
+                     (good_off[:2], good_ids), (None, good_ids)):
+        with pytest.raises(ValueError):
+            s.sample(x, prm, off, ids, u)
+
+
+def test_noalloc_status_reader_is_exported():
+    lib = _lib.load()
+    assert hasattr(lib, "lss_noalloc_read_status")
+    assert lib.lss_noalloc_read_status(None, None) == 1   # NULL output: rejected without device work

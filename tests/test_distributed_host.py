@@ -52,3 +52,16 @@ def test_row_and_vocab_exchange_gloo_world2(tmp_path):
         assert r["rows"] == r["rows_ref"]
         assert r["vocab"] == r["vocab_ref"]
     assert res[0]["vocab"] == res[1]["vocab"]
+
+
+def test_vocab_mode_rejects_rows_it_cannot_serve():
+    import torch
+    from localstrm_b200.distributed import VocabShardSampler
+    s = VocabShardSampler("cpu", K=64, records=lambda *a: None, merge=lambda *a: None, record_bytes=528)
+    s.check_params(top_k=[64, 64], min_p=[0.0, 1.0], repetition_penalty=[1.0, 1.0],
+                   frequency_penalty=torch.zeros(2), presence_penalty=[0.0, 0.0])
+    for bad in (dict(top_k=[64, 20]), dict(top_k=[-1, 64]), dict(min_p=[0.0, 0.05]),
+                dict(repetition_penalty=[1.0, 1.1]), dict(frequency_penalty=[0.0, 0.3]),
+                dict(presence_penalty=torch.tensor([0.2, 0.0]))):
+        with pytest.raises(ValueError):
+            s.check_params(**bad)

@@ -79,6 +79,41 @@ def test_vocab_shards_match_oracle(n):
 
 
 @needs_cuda
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_config5_full_size_emulated_shards(n):
+    """Config 5 at its stated size (B=128, V=256,000, top-k 64, top-p 0.9) split into n column
+    shards of one buffer: every record byte for byte against the oracle, then the merged kept
+    set, probabilities and draw of every row against the oracle on the whole row."""
+    lib = _lib.load()
+    K = 64
+    w = wl.config5(seed=0)
+    assert (w.B, w.V) == (128, 256_000)
+    x = torch.from_numpy(w.logits).cuda()
+    gathered, T = _gpu_records(lib, x, w, n, K)
+    rb = lib.lss_shard_record_bytes(K)
+    g = gathered.cpu().numpy().reshape(n, w.B, rb)
+    for s in range(n):
+        off, stop = shard_vocab(w.V, n, s)
+        ref = OS.shard_records(w.logits[:, off:stop], off, w.temperature, K).reshape(w.B, rb)
+        assert np.array_equal(g[s, :, :8 * K + 4], ref[:, :8 * K + 4]), s          # codes, max
+        assert np.array_equal(g[s, :, 8 * K + 8:], ref[:, 8 * K + 8:]), s          # flags, count
+        se, se_ref = g[s, :, 8 * K + 4:8 * K + 8].view(np.float32), ref[:, 8 * K + 4:8 * K + 8].view(np.float32)
+        assert np.allclose(se, se_ref, rtol=1e-5), s
+    tok, kept, probs = _merge(lib, gathered, w, n, K, T)
+    for b in range(w.B):
+        res = R.sample_row(w.logits[b], float(w.temperature[b]), top_k=K, top_p=float(w.top_p[b]),
+                           u=float(w.uniforms[b]))
+        assert P.compare_kept(w, b, kept[b], res.kept, res) == "", b
+        assert kept[b][int(tok[b])], b
+        both = kept[b] & res.kept
+        assert P.probs_close(probs[b], res.probs, both) <= P.PROB_RTOL, b
+        own = R.draw_inverse_cdf(kept[b], np.where(kept[b], probs[b], 0).astype(np.float32), float(w.uniforms[b]))
+        assert int(tok[b]) == own or P.draw_is_boundary(np.where(kept[b], probs[b], 0), float(w.uniforms[b])), b
+        if int(tok[b]) != res.token:
+            assert P.draw_is_boundary(res.probs, float(w.uniforms[b])), (b, int(tok[b]), res.token)
+
+
+@needs_cuda
 def test_vocab_shards_special_rows():
     lib = _lib.load()
     K, n = 32, 4

@@ -57,3 +57,8 @@ def test_noalloc_matches_workspace_entry_point_twice():
         assert np.array_equal(got[1], ref[1]), w.name
         assert np.array_equal(got[2], ref[2]), w.name
         assert (got[0] >= 0).all() and (got[0] < w.V).all()
+        # The device status of the call (error flags in the fixed scratch) reads clean.
+        import ctypes
+        flags = ctypes.c_uint32(0xdead)
+        st = lib.lss_noalloc_read_status(ctypes.byref(flags), torch.cuda.current_stream().cuda_stream)
+        assert st == 0 and flags.value == 0, (w.name, st, flags.value)
