@@ -421,7 +421,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     graphs[0].replay()
     torch.cuda.synchronize()
 
-    # roofline of the dominant kernel (the streaming pass, lss_scan_kernel)
+    # roofline of the dominant kernel (the streaming pass, lss_stream_kernel)
     alg = algorithmic_bytes(w)
     kern_avg_ms = statistics.mean(kern_ms)
     achieved = alg / (kern_avg_ms / 1000.0) / 1e9
@@ -430,7 +430,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if args.workload == "headline" and os.path.exists(tp):
         try:
-            traffic = json.load(open(tp)).get("lss_scan_kernel_headline_bytes_per_launch")
+            traffic = json.load(open(tp)).get("lss_stream_kernel_headline_bytes_per_launch")
         except (OSError, ValueError):
             traffic = None
 
@@ -503,7 +503,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "hbm_gbs": alg * world * n_steps_total / (elapsed_ms / 1000.0) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "lss_scan_kernel", "peak_source": peak_kind,
+                         "kernel": "lss_stream_kernel", "peak_source": peak_kind,
                          "algorithmic_bytes_per_launch": alg, "kernel_ms": kern_avg_ms},
             "step_ms_median": statistics.median(step_ms_each),
             "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,

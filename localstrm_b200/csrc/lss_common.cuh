@@ -113,6 +113,19 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
   return true;
 }
+// Bounded wait of a whole warp (all 32 lanes call it together): every lane tests the phase
+// (so that each lane acquires the data the phase publishes) and the loop exits for all lanes at
+// once, so that no lane spins on its own while the others wait at a warp-synchronous
+// instruction.  Returns false (for every lane) after WAIT_CYCLES of lane 0's clock.
+__device__ __forceinline__ bool warp_mbar_wait(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  for (;;) {
+    const bool ok = mbar_try_wait(bar, parity);
+    if (__all_sync(0xffffffffu, ok)) return true;
+    const int late = (threadIdx.x & 31) == 0 && clock64() - t0 > WAIT_CYCLES;
+    if (__shfl_sync(0xffffffffu, late, 0)) return false;
+  }
+}
 // Bounded wait that lets the thread sleep until the phase completes (suspend-time hint), for
 // waits that are not on the critical path of the waiting warp.
 __device__ __forceinline__ bool mbar_wait_bounded_sleep(uint64_t* bar, uint32_t parity) {

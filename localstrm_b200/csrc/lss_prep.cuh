@@ -15,7 +15,7 @@
 namespace lss {
 
 constexpr int PREP_SMEM_SLOTS = 4096;   // histories up to 2,048 ids hash in shared memory
-constexpr int PREP_MAXSEG = 32;         // slices per row
+constexpr int PREP_MAXSEG = 320;        // slices (segments) per row: a row of 327,680 logits in 1,024-logit segments
 constexpr uint32_t EMPTY = 0xffffffffu;
 
 struct PrepOut {
@@ -28,19 +28,20 @@ struct PrepOut {
 // row's penalties apply (otherwise only empty segments are written).
 constexpr int PREP_SCRATCH_WORDS = 2 * PREP_SMEM_SLOTS + PREP_SMEM_SLOTS / 4 + 2 * (PREP_MAXSEG + 1) + 1;
 
+// The segment offsets written are relative to the row's first pair, plus `so_base`.
 template <int NTH, class Sync>
 __device__ void prep_row(const RowArgs& a, int row, bool active, int TE, int nseg, const PrepOut& o, uint32_t* sw,
-                         Sync sync) {
+                         Sync sync, int so_base = 0) {
   const int tid = threadIdx.x, lane = tid & 31;
   if (!active) {
-    if (tid <= nseg) o.so[tid] = 0;
+    for (int t = tid; t <= nseg; t += NTH) o.so[t] = so_base;
     return;
   }
   int b = 0, e = 0;
   if (!hist_range(a.hist_off, row, a.H, b, e)) atomicOr(o.bad, LSS_FLAG_BAD_HISTORY);
   const int H = e - b;
   if (H <= 0) {
-    if (tid <= nseg) o.so[tid] = 0;
+    for (int t = tid; t <= nseg; t += NTH) o.so[t] = so_base;
     return;
   }
   uint32_t* skeys = sw;
@@ -65,9 +66,9 @@ __device__ void prep_row(const RowArgs& a, int row, bool active, int TE, int nse
     keys[s] = EMPTY;
     cnts[s] = 0;
   }
-  if (tid <= PREP_MAXSEG) {
-    bcnt[tid] = 0;
-    bfill[tid] = 0;
+  for (int t = tid; t <= PREP_MAXSEG; t += NTH) {
+    bcnt[t] = 0;
+    bfill[t] = 0;
   }
   if (tid == 0) *nlist = 0;
   sync();
@@ -157,7 +158,7 @@ __device__ void prep_row(const RowArgs& a, int row, bool active, int TE, int nse
       a.uniq_cnt[b + pos] = (int32_t)cnts[s];
     }
   }
-  if (tid <= nseg) o.so[tid] = (int32_t)bcnt[tid];
+  for (int t = tid; t <= nseg; t += NTH) o.so[t] = so_base + (int32_t)bcnt[t];
 }
 
 struct BlockSync {
@@ -166,8 +167,10 @@ struct BlockSync {
 
 // =========================================================================================
 // K0: history kernel — one CTA per row: the (id, count) pairs of the rows whose penalties
-// the scan kernel applies, grouped by its slices (seg2[row][0 .. S]); a per-row flag for ids
-// outside [0, V).  Block 0 clears the workspace status first (no other block writes it).
+// apply, grouped by segments of TS logits (seg2[row][0 .. S] hold the absolute offsets of each
+// segment's pairs in the pair arrays, so the streaming kernel finds a chunk's pairs directly);
+// a per-row flag for ids outside [0, V) or a bad offset range.  Block 0 clears the workspace
+// status first (no other block writes it).
 // Histories of up to PREP_SMEM_SLOTS / 2 ids take a short path: the ids are requested before
 // the table is cleared, slice counts are taken as new keys enter, and one pass over the list
 // of occupied slots scatters the pairs; longer ones go through prep_row's global table.
@@ -177,7 +180,7 @@ constexpr int HIST_NT = 1024;
 struct HistArgs {
   RowArgs r;
   int S, TS;
-  int32_t* seg2;        // [B][S + 1]
+  int32_t* seg2;        // [B][S + 1]: absolute pair offsets per segment
   uint32_t* rowflag;    // [B]
   uint32_t* header;     // 64 words
 };
@@ -211,7 +214,7 @@ __global__ void __launch_bounds__(HIST_NT) lss_hist_kernel(const HistArgs h) {
   }
   if (2 * H > PREP_SMEM_SLOTS) {
     __syncthreads();  // rowflag cleared before prep_row may raise it
-    prep_row<HIST_NT>(a, row, true, h.TS, nseg, o, sw, BlockSync());
+    prep_row<HIST_NT>(a, row, true, h.TS, nseg, o, sw, BlockSync(), b);
     return;
   }
   // ---- short path: at most 2 ids per thread
@@ -278,18 +281,27 @@ __global__ void __launch_bounds__(HIST_NT) lss_hist_kernel(const HistArgs h) {
     }
   }
   __syncthreads();
-  if (tid < 32) {
-    // Exclusive scan of the slice counts (lane c holds slice c; nseg <= 32).
-    const uint32_t v = lane < nseg ? bcnt[lane] : 0u;
+  {
+    // Exclusive scan of the segment counts (thread c holds segment c; nseg <= PREP_MAXSEG <
+    // HIST_NT), written back relative to the row and to seg2 absolute.
+    __shared__ uint32_t wsum[HIST_NT / 32];
+    const int warp = tid >> 5;
+    const uint32_t v = tid < nseg ? bcnt[tid] : 0u;
     uint32_t incl = v;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const uint32_t y = __shfl_up_sync(0xffffffffu, incl, d);
       if (lane >= d) incl += y;
     }
-    bcnt[lane] = incl - v;
-    if (lane <= nseg) so[lane] = (int32_t)(incl - v);
-    if (lane == 31 && nseg == 32) so[32] = (int32_t)incl;
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    uint32_t pre = 0;
+    for (int q = 0; q < warp; ++q) pre += wsum[q];
+    const uint32_t ex = pre + incl - v;
+    if (tid <= nseg) {
+      if (tid < nseg) bcnt[tid] = ex;
+      so[tid] = b + (int32_t)ex;   // tid == nseg: the row's total
+    }
   }
   __syncthreads();
   const uint32_t L = *nlist;

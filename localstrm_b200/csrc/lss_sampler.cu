@@ -1,9 +1,10 @@
 // lss_sampler.cu — batched token sampler for B200 (sm_100a): the one translation unit of
 // liblss.so.  It holds the C ABI of include/lsampler.h and the host-side launch logic; the
 // kernels live in the headers it includes:
-//   lss_prep.cuh   K0  history (id, count) pairs per slice; K3's per-row preparation
-//   lss_scan.cuh   K1  persistent streaming pass over the logits (the hot path)
-//   lss_resolve.cuh K2 per-row gather of K1's candidates, sort / top-k / top-p / draw
+//   lss_prep.cuh   K0  history (id, count) pairs per 1,024-logit segment; K3's per-row preparation
+//   lss_stream.cuh K1  persistent streaming pass over the logits (the hot path)
+//   lss_resolve.cuh K2 per-row gather of K1's candidates and history values, sort / top-k /
+//                      top-p / draw
 //   lss_slow.cuh   K3  rows K2 defers (dense radix select, NaN guard)
 //   lss_shard.cuh      vocabulary-sharded mode: per-shard top-K records, merge and draw
 //   lss_common.cuh     keys, PTX wrappers, reductions
@@ -24,7 +25,7 @@
 #include "lsampler.h"
 #include "lss_common.cuh"
 #include "lss_prep.cuh"
-#include "lss_scan.cuh"
+#include "lss_stream.cuh"
 #include "lss_resolve.cuh"
 #include "lss_slow.cuh"
 #include "lss_shard.cuh"
@@ -125,11 +126,23 @@ constexpr int MAX_VOCAB = MAXCL * (TILE_MAX_BYTES / 4);
 static int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
 struct Plan {
-  int S, TS, SEG;             // scan kernel: slices per row, logits per slice, candidate slots per item
-  int scan_tile, scan_smem;   // scan kernel: tile bytes per stage, dynamic shared memory
+  int nseg;                   // history segments per row (SEGV logits each)
+  int MAXSL;                  // slices per row the workspace reserves (either logit width)
   int CL, TE;                 // second kernel: CTAs per row, logits per CTA
   int slow_tile, slow_smem;
 };
+
+// Streaming kernel: chunks per row for logits of `es` bytes.
+static int chunks_per_row(int V, int es) { return (V + ST_CB / es - 1) / (ST_CB / es); }
+
+// Most CTA ranges one row can intersect when B * C chunks are split over at most ST_GCAP CTAs:
+// every range holds at least floor(N / G) chunks.
+static int max_slices(int B, int C) {
+  const int64_t N = (int64_t)std::max(B, 1) * C;
+  const int64_t G = std::min<int64_t>(ST_GCAP, N);
+  const int64_t P = N / G;
+  return (int)std::min<int64_t>(C, (C - 1 + P - 1) / P + 1);
+}
 
 static int slow_extra(int CL) {
   switch (CL) {
@@ -140,17 +153,10 @@ static int slow_extra(int CL) {
   }
 }
 
-static Plan make_plan(int V) {
+static Plan make_plan(int B, int V) {
   Plan pl{};
-  // Slices as large as the compute threads' registers and the copy ring allow.
-  const int fixed = scan_smem_bytes(0) - SC_NST * scan_stage_bytes(0);
-  const int tile_cap = ((SC_SMEM_MAX - fixed) / SC_NST - SC_HB * 4) / 128 * 128;
-  const int ts_max = std::min(SC_TS_MAX, tile_cap / 4 / 16 * 16);
-  pl.S = (V + ts_max - 1) / ts_max;
-  pl.TS = round_up((V + pl.S - 1) / pl.S, 16);
-  pl.SEG = std::max(SC_SEG_MIN, FAST_CAP / pl.S);
-  pl.scan_tile = round_up(pl.TS * 4, 128);
-  pl.scan_smem = scan_smem_bytes(pl.scan_tile);
+  pl.nseg = (V + SEGV - 1) / SEGV;
+  pl.MAXSL = std::max(max_slices(B, chunks_per_row(V, 4)), max_slices(B, chunks_per_row(V, 2)));
   int CL = 1;
   while (CL < MAXCL && round_up((V + CL - 1) / CL, 16) * 4 > TILE_TARGET_BYTES) CL <<= 1;
   pl.CL = CL;
@@ -161,31 +167,33 @@ static Plan make_plan(int V) {
 }
 
 // Workspace: header (word 0 error flags, word 2 deferred-row count), row path codes, the
-// scan kernel's item summaries and candidate segments, the per-slice segments of the unique
-// history pairs (for the second kernel's slices and for the scan kernel's), per-row history
-// flags, the deferred-row list, the pair arrays and the global hash table for rows with long
-// histories.  row_path sits at a fixed offset.
+// streaming kernel's slice summaries and candidate segments, the per-slice segments of the
+// unique history pairs for the second kernel and the per-segment offsets for the streaming
+// kernel, per-row history flags, the deferred-row list, the pair arrays (ids, counts, raw
+// logits) and the global hash table for rows with long histories.  row_path sits at a fixed
+// offset.
 struct WsLayout {
-  size_t header, row_path, summ, cand, seg_off, seg2, rowflag, defer_rows, uniq_ids, uniq_cnt, gkeys, gcnts,
-      total;
+  size_t header, row_path, summ, cand, seg_off, seg2, rowflag, defer_rows, uniq_ids, uniq_cnt, hraw, gkeys,
+      gcnts, total;
 };
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 static WsLayout ws_layout(int B, int V, int64_t H) {
   WsLayout L{};
   const size_t b = (size_t)std::max(B, 1), h = (size_t)std::max<int64_t>(H, 1);
-  const Plan pl = make_plan(std::max(V, 1));
-  const size_t items = b * (size_t)pl.S;
+  const Plan pl = make_plan(std::max(B, 1), std::max(V, 1));
+  const size_t slices = b * (size_t)pl.MAXSL;
   size_t o = 0;
   L.header = o; o += 256;
   L.row_path = o; o = align256(o + 4 * b);
-  L.summ = o; o = align256(o + 16 * items);
-  L.cand = o; o = align256(o + 8 * items * (size_t)pl.SEG);
+  L.summ = o; o = align256(o + 16 * slices);
+  L.cand = o; o = align256(o + 8 * slices * (size_t)ST_SEGCAP);
   L.seg_off = o; o = align256(o + 4 * b * (MAXCL + 1));
-  L.seg2 = o; o = align256(o + 4 * b * (size_t)(pl.S + 1));
+  L.seg2 = o; o = align256(o + 4 * b * (size_t)(pl.nseg + 1));
   L.rowflag = o; o = align256(o + 4 * b);
   L.defer_rows = o; o = align256(o + 4 * b);
-  L.uniq_ids = o; o = align256(o + 4 * (h + 4));   // 4 entries of padding: 16-byte copy windows
+  L.uniq_ids = o; o = align256(o + 4 * (h + 4));
   L.uniq_cnt = o; o = align256(o + 4 * (h + 4));
+  L.hraw = o; o = align256(o + 4 * (h + 4));
   L.gkeys = o; o = align256(o + 8 * h);
   L.gcnts = o; o = align256(o + 8 * h);
   L.total = o;
@@ -205,9 +213,14 @@ static int current_device() {
   return dev;
 }
 
+// The per-(kernel, device) caches are filled on first use; one lock serialises that, so host
+// threads that make their first calls at the same time do not race on them.
+static std::mutex g_cfg_mu;
+
 template <class K>
 static cudaError_t prepare_cluster_kernel(K kern, KernelCfg& kc, int CL, int smem, int& nclusters) {
   const int dev = current_device();
+  std::lock_guard<std::mutex> lock(g_cfg_mu);
   if (kc.smem[dev] < smem) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -237,21 +250,23 @@ static cudaError_t prepare_cluster_kernel(K kern, KernelCfg& kc, int CL, int sme
   return cudaSuccess;
 }
 
-// Persistent grid of the scan kernel: every CTA that fits (one per SM at this shared memory).
+// Persistent grid of the streaming kernel: every CTA that fits (one per SM at this shared
+// memory), at most ST_GCAP.
 template <class K>
-static cudaError_t prepare_scan_kernel(K kern, KernelCfg& kc, int smem, int& nctas) {
+static cudaError_t prepare_stream_kernel(K kern, KernelCfg& kc, int smem, int& nctas) {
   const int dev = current_device();
+  std::lock_guard<std::mutex> lock(g_cfg_mu);
   if (kc.smem[dev] < smem) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     int per_sm = 0, nsm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, SC_NT, (size_t)smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, ST_NT, (size_t)smem);
     if (e != cudaSuccess) return e;
     e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
     if (per_sm <= 0) return cudaErrorInvalidConfiguration;
     kc.smem[dev] = smem;
-    kc.count[dev] = per_sm * nsm;
+    kc.count[dev] = std::min(per_sm * nsm, ST_GCAP);
   }
   nctas = kc.count[dev];
   return cudaSuccess;
@@ -289,19 +304,19 @@ static cudaError_t launch_clusters(K kern, const RowArgs& a, int CL, int ncluste
   return launch_pdl(kern, (unsigned)(nclusters * CL), (unsigned)NT, (size_t)smem, CL, st, a);
 }
 
-// K1 (scan), K2 (resolve, one CTA per row), K3 (second kernel over the deferred list).
+// K1 (streaming pass), K2 (resolve, one CTA per row), K3 (second kernel over the deferred list).
 template <int DT>
-static cudaError_t launch_rows(const ScanArgs& sa, const RowArgs& ra, const GatherArgs& ga, const Plan& pl, int B,
+static cudaError_t launch_rows(StreamArgs sa, const RowArgs& ra, GatherArgs ga, const Plan& pl, int B,
                                cudaStream_t st, bool scan_only) {
-  static KernelCfg scan_cfg{};
+  static KernelCfg stream_cfg{};
   int nctas = 0;
-  // 16-bit logits: half-size stages plus an f32 work tile (the same total as f32 stages).
-  const int smem = DT == LSS_DTYPE_F32 ? pl.scan_smem : scan_smem_bytes(sa.tile_bytes, sa.work_bytes);
-  cudaError_t e = prepare_scan_kernel(lss_scan_kernel<DT>, scan_cfg, smem, nctas);
+  constexpr int smem = stream_smem_bytes();
+  cudaError_t e = prepare_stream_kernel(lss_stream_kernel<DT>, stream_cfg, smem, nctas);
   if (e != cudaSuccess) return e;
-  const int nitems = B * pl.S;
-  e = launch_pdl(lss_scan_kernel<DT>, (unsigned)std::min(nctas, nitems), (unsigned)SC_NT, (size_t)smem, 1,
-                 st, sa);
+  const int G = (int)std::min<int64_t>(nctas, sa.N);
+  // Both kernels derive a row's slices from the same split of the N chunks over G CTAs.
+  ga.G = G;
+  e = launch_pdl(lss_stream_kernel<DT>, (unsigned)G, (unsigned)ST_NT, (size_t)smem, 1, st, sa);
   if (e != cudaSuccess || scan_only) return e;
   e = launch_pdl(lss_resolve_kernel, (unsigned)B, (unsigned)NT, (size_t)0, 1, st, ra, ga);
   if (e != cudaSuccess) return e;
@@ -420,7 +435,7 @@ int lss_sample_prepare(int B, int V, const float* temperature, const int32_t* to
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   unsigned char* ws = reinterpret_cast<unsigned char*>(workspace);
   const WsLayout L = ws_layout(B, V, hist_total);
-  const Plan pl = make_plan(V);
+  const Plan pl = make_plan(B, V);
   HistArgs h{};
   h.r.B = B;
   h.r.V = V;
@@ -438,8 +453,8 @@ int lss_sample_prepare(int B, int V, const float* temperature, const int32_t* to
   h.r.uniq_cnt = reinterpret_cast<int32_t*>(ws + L.uniq_cnt);
   h.r.gkeys = reinterpret_cast<uint32_t*>(ws + L.gkeys);
   h.r.gcnts = reinterpret_cast<uint32_t*>(ws + L.gcnts);
-  h.S = pl.S;
-  h.TS = pl.TS;
+  h.S = pl.nseg;
+  h.TS = SEGV;
   h.seg2 = reinterpret_cast<int32_t*>(ws + L.seg2);
   h.rowflag = reinterpret_cast<uint32_t*>(ws + L.rowflag);
   h.header = reinterpret_cast<uint32_t*>(ws + L.header);
@@ -466,37 +481,28 @@ static int sample_rows(const void* logits, int dtype, int B, int V, int64_t row_
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   unsigned char* ws = reinterpret_cast<unsigned char*>(workspace);
   const WsLayout L = ws_layout(B, V, hist_total);
-  const Plan pl = make_plan(V);
+  const Plan pl = make_plan(B, V);
   if (kept_out && cudaMemsetAsync(kept_out, 0, (size_t)B * V, st) != cudaSuccess) return LSS_ERR_CUDA;
   if (probs_out && cudaMemsetAsync(probs_out, 0, (size_t)B * V * sizeof(float), st) != cudaSuccess)
     return LSS_ERR_CUDA;
   uint32_t* header = reinterpret_cast<uint32_t*>(ws + L.header);
-  ScanArgs sa{};
+  const int es = dtype == LSS_DTYPE_F32 ? 4 : 2;
+  StreamArgs sa{};
   sa.logits = logits;
   sa.row_stride = row_stride;
   sa.B = B;
   sa.V = V;
-  sa.S = pl.S;
-  sa.TS = pl.TS;
-  sa.SEG = pl.SEG;
-  if (dtype == LSS_DTYPE_F32) {
-    sa.tile_bytes = pl.scan_tile;
-    sa.work_bytes = 0;
-  } else {
-    sa.tile_bytes = round_up(pl.TS * 2, 128);
-    sa.work_bytes = pl.scan_tile;  // TS f32 values
-  }
+  sa.C = chunks_per_row(V, es);
+  sa.N = (int64_t)B * sa.C;
+  sa.MAXSL = pl.MAXSL;
+  sa.nseg = pl.nseg;
   sa.use_hist = hist_total > 0 ? 1 : 0;
   sa.temperature = temperature;
   sa.top_k = top_k;
   sa.min_p = min_p;
-  sa.rep = repetition_penalty;
-  sa.freq = frequency_penalty;
-  sa.pres = presence_penalty;
-  sa.hist_off = hist_offsets;
-  sa.uniq_ids = reinterpret_cast<const int32_t*>(ws + L.uniq_ids);
-  sa.uniq_cnt = reinterpret_cast<const int32_t*>(ws + L.uniq_cnt);
   sa.seg2 = reinterpret_cast<const int32_t*>(ws + L.seg2);
+  sa.uniq_ids = reinterpret_cast<const int32_t*>(ws + L.uniq_ids);
+  sa.hraw = reinterpret_cast<float*>(ws + L.hraw);
   sa.summ = reinterpret_cast<uint4*>(ws + L.summ);
   sa.cand = reinterpret_cast<uint64_t*>(ws + L.cand);
   sa.err = header;
@@ -535,8 +541,14 @@ static int sample_rows(const void* logits, int dtype, int B, int V, int64_t row_
   GatherArgs ga{};
   ga.summ = sa.summ;
   ga.cand = sa.cand;
-  ga.S = pl.S;
-  ga.SEG = pl.SEG;
+  ga.MAXSL = pl.MAXSL;
+  ga.SEGCAP = ST_SEGCAP;
+  ga.C = sa.C;
+  ga.N = sa.N;
+  ga.G = 1;  // set at launch to the streaming kernel's grid
+  ga.nseg = pl.nseg;
+  ga.seg2 = sa.seg2;
+  ga.hraw = sa.hraw;
   ga.rowflag = reinterpret_cast<const uint32_t*>(ws + L.rowflag);
   cudaError_t e;
   switch (dtype) {
