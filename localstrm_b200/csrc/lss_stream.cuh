@@ -32,6 +32,8 @@
 // filter, which the resolve kernel applies.
 #pragma once
 
+#include <type_traits>
+
 #include "lss_common.cuh"
 
 namespace lss {
@@ -46,6 +48,7 @@ constexpr int ST_ROWTAB = 64;                 // rows whose parameters a CTA kee
 constexpr int ST_GCAP = 160;                  // largest grid the workspace layout allows for
 constexpr int SEGV = 1024;                    // history segment: K0 groups the pairs per SEGV logits
 constexpr int ST_STAGE_BYTES = ST_NW * ST_R * ST_CB;
+constexpr int ST_XMW = ST_CB / 2 / 32;        // words of a warp's exclusion map (one bit per logit)
 
 constexpr int ITEM_SKIP = 1, ITEM_GREEDY = 2, ITEM_SAMPLE = 3;
 // Summary flags: NaN / +inf among the slice's non-history values.
@@ -72,7 +75,8 @@ struct __align__(16) RowPrm {
   float tl;             // min-p active: T * ln(min_p), the floor's offset in z; else 0
   float sb;             // 16 / T: bins of the top-k histogram per unit of z
   float binw;           // T / 16
-  int pad[2];
+  int jsl;              // index of this CTA's slice among the row's slices
+  int nch;              // chunks of the row in this CTA's range
 };
 
 struct StreamArgs {
@@ -95,7 +99,8 @@ struct StreamArgs {
 };
 
 __host__ __device__ constexpr int stream_smem_bytes() {
-  return ST_STAGE_BYTES + ST_NSLOT * (int)sizeof(SliceSlot) + ST_NW * ST_R * 8 + ST_ROWTAB * (int)sizeof(RowPrm) + 16;
+  return ST_STAGE_BYTES + ST_NSLOT * (int)sizeof(SliceSlot) + ST_NW * ST_R * 8 + ST_ROWTAB * (int)sizeof(RowPrm) + 16 +
+         ST_NW * ST_XMW * 4;
 }
 
 // Largest CTA index whose range starts at or before chunk x (ranges [c N / G, (c + 1) N / G)).
@@ -104,8 +109,12 @@ __host__ __device__ __forceinline__ int cta_of_chunk(int64_t x, int64_t N, int G
   return (int)(c < G - 1 ? c : G - 1);
 }
 
-__device__ __forceinline__ RowPrm make_row_prm(const StreamArgs& a, int row) {
+// Parameters of `row` as the CTA whose range is [g0, g1) of N chunks (G CTAs) sees it.
+__device__ __forceinline__ RowPrm make_row_prm(const StreamArgs& a, int row, int64_t g0, int64_t g1) {
   RowPrm p{};
+  const int64_t rs = (int64_t)row * a.C;
+  p.jsl = (int)blockIdx.x - cta_of_chunk(rs, a.N, (int)gridDim.x);
+  p.nch = (int)(min(g1, rs + a.C) - max(g0, rs));
   const float T = a.temperature[row];
   const int k = a.top_k[row];
   const float mp = a.min_p[row];
@@ -141,6 +150,8 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
   // own copies in flight and returns, with the error flag raised.
   volatile uint32_t* abort_w = reinterpret_cast<volatile uint32_t*>(rtab + ST_ROWTAB);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Per warp: one bit per logit of the current chunk, set for the history positions.
+  uint32_t* xm = reinterpret_cast<uint32_t*>(rtab + ST_ROWTAB) + 4 + warp * ST_XMW;
   const int G = gridDim.x;
   const int64_t N = a.N;
   const int64_t g0 = (int64_t)blockIdx.x * N / G, g1 = (int64_t)(blockIdx.x + 1) * N / G;
@@ -154,25 +165,41 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
     for (int i = tid; i < ST_NSLOT * W; i += ST_NT) sw[i] = (i % W == 0) ? (uint32_t)(i / W) : 0u;
     if (tid < ST_NW * ST_R) mbar_init(&bars[tid], 1);
     for (int i = tid; i < ST_ROWTAB; i += ST_NT)
-      if (row0 + i < a.B) rtab[i] = make_row_prm(a, row0 + i);
+      if (row0 + i < a.B) rtab[i] = make_row_prm(a, row0 + i, g0, g1);
     if (tid < ST_NW * ST_R) fence_barrier_init();
     if (tid == 0) *abort_w = 0u;
+    for (int q = tid; q < ST_NW * ST_XMW; q += ST_NT) reinterpret_cast<uint32_t*>(rtab + ST_ROWTAB)[4 + q] = 0u;
   }
   __syncthreads();
   pdl_trigger();  // the resolve kernel may launch; it waits for this grid before reading
 
   auto prm_of = [&](int row) -> RowPrm {
-    return row - row0 < ST_ROWTAB ? rtab[row - row0] : make_row_prm(a, row);
+    return row - row0 < ST_ROWTAB ? rtab[row - row0] : make_row_prm(a, row, g0, g1);
   };
   uint64_t* wbar = bars + warp * ST_R;
   unsigned char* wst = smem + (size_t)warp * ST_R * ST_CB;
   const int64_t gw = g0 + warp;
+  // Positions (row, chunk of the row) are carried forward by adding chunks, so that the loop
+  // divides only when it crosses into another row.
+  struct Pos {
+    int row, c;
+  };
+  auto adv = [&](Pos p, int k) -> Pos {
+    p.c += k;
+    if (p.c >= C) {
+      const int q = p.c / C;
+      p.row += q;
+      p.c -= q * C;
+    }
+    return p;
+  };
+  const Pos pw{(int)(gw / C), (int)(gw - (gw / C) * C)};
 
-  // Lane 0: start the copy of chunk g into stage s (an arrival without bytes for a skipped row
-  // or a misaligned chunk, whose logits the warp loads itself).
-  auto issue = [&](int64_t g, int s) {
-    const int row = (int)(g / C);
-    const int lo = (int)(g - (int64_t)row * C) * CE;
+  // Lane 0: start the copy of chunk g (at position p) into stage s (an arrival without bytes for
+  // a skipped row or a misaligned chunk, whose logits the warp loads itself).
+  auto issue = [&](Pos p, int s) {
+    const int row = p.row;
+    const int lo = p.c * CE;
     const int n = min(CE, V - lo);
     const char* src = reinterpret_cast<const char*>(a.logits) + ((int64_t)row * a.row_stride + lo) * ES;
     const int mode = prm_of(row).mode;
@@ -183,7 +210,7 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
   // The first chunks stream in while K0 still runs: they read nothing K0 writes.
   if (lane == 0)
     for (int i = 0; i < ST_R; ++i)
-      if (gw + (int64_t)i * ST_NW < g1) issue(gw + (int64_t)i * ST_NW, i);
+      if (gw + (int64_t)i * ST_NW < g1) issue(adv(pw, i * ST_NW), i);
   __syncwarp();
   pdl_wait();  // K0's pairs and segment offsets are complete and visible
 
@@ -201,6 +228,24 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
     if (DT == LSS_DTYPE_F32) reinterpret_cast<float*>(st)[i] = reinterpret_cast<const float*>(src)[i];
     else reinterpret_cast<uint16_t*>(st)[i] = reinterpret_cast<const uint16_t*>(src)[i];
   };
+  // Sets the logits of one 16-byte vector whose bit in `bits` is set to -inf.
+  auto exclude = [&](uint4& r, uint32_t bits) {
+    uint32_t w[4] = {r.x, r.y, r.z, r.w};
+    if (DT == LSS_DTYPE_F32) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if ((bits >> q) & 1u) w[q] = 0xff800000u;
+    } else {
+      const uint32_t ni = DT == LSS_DTYPE_BF16 ? 0xff80u : 0xfc00u;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if ((bits >> (2 * q)) & 1u) w[q] = (w[q] & 0xffff0000u) | ni;
+        if ((bits >> (2 * q + 1)) & 1u) w[q] = (w[q] & 0x0000ffffu) | (ni << 16);
+      }
+    }
+    r = make_uint4(w[0], w[1], w[2], w[3]);
+  };
+  using MaskT = typename std::conditional<(NV * VPV > 32), unsigned long long, uint32_t>::type;
   // The logits of 16-byte vector q of a stage, widened to f32.
   auto widen = [&](const uint4 r, float* x) {
     const uint32_t w[4] = {r.x, r.y, r.z, r.w};
@@ -221,27 +266,62 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
     }
   };
 
+  // History pairs of chunk gg: absolute offsets [q0, q1) into the pair arrays (K0 grouped them
+  // by SEGV-logit segments, and chunks start on segment boundaries).
+  auto offs_of = [&](int64_t gg, Pos p, int& q0, int& q1) {
+    q0 = q1 = 0;
+    if (gg < g1 && a.use_hist) {
+      const int r = p.row;
+      if (prm_of(r).mode == ITEM_SAMPLE) {
+        const int l0 = p.c * CE;
+        const int nn = min(CE, V - l0);
+        const int32_t* so = a.seg2 + (int64_t)r * (a.nseg + 1);
+        q0 = so[l0 / SEGV];
+        q1 = so[min(a.nseg, (l0 + nn + SEGV - 1) / SEGV)];
+      }
+    }
+  };
+  // The first PF * 32 history ids of a chunk are fetched one chunk ahead, its offsets two chunks
+  // ahead, so that their latency hides behind the chunk before.
+  constexpr int PF = 8;
+  auto ids_of = [&](int q0, int q1, int* idv) {
+#pragma unroll
+    for (int k = 0; k < PF; ++k) {
+      const int e = q0 + lane + 32 * k;
+      idv[k] = e < q1 ? a.uniq_ids[e] : -1;
+    }
+  };
+  // Stage s of chunk g is no longer read: generic writes to it precede the next bulk copy into it.
+  auto release = [&](int64_t g, Pos pi, int s, bool wrote) {
+    if (wrote) fence_proxy_async();
+    __syncwarp();
+    if (lane == 0 && g + (int64_t)ST_R * ST_NW < g1) issue(pi, s);
+  };
+
   const int nwch = gw < g1 ? (int)((g1 - gw + ST_NW - 1) / ST_NW) : 0;  // this warp's chunks
+  int c0, c1, n0, n1;  // pair offsets of this chunk and of the next one
+  int idc[PF];         // ids of this chunk's first pairs
+  Pos pc = pw;                       // this chunk
+  Pos p2 = adv(pw, 2 * ST_NW);        // two chunks on (history offsets)
+  Pos pr = adv(pw, ST_R * ST_NW);     // ST_R chunks on (the copy started when this one is released)
+  offs_of(gw, pc, c0, c1);
+  offs_of(gw + ST_NW, adv(pw, ST_NW), n0, n1);
+  ids_of(c0, c1, idc);
   int i = 0;
+  int s = 0;
+  uint32_t par = 0;
   for (;; ++i) {
     const int64_t g = gw + (int64_t)i * ST_NW;
     if (g >= g1 || __shfl_sync(0xffffffffu, lane == 0 ? *abort_w : 0u, 0)) break;
-    const int s = i % ST_R;
-    const uint32_t par = (uint32_t)((i / ST_R) & 1);
-    const int row = (int)(g / C);
-    const int c = (int)(g - (int64_t)row * C);
-    const int lo = c * CE;
+    const int row = pc.row;
+    const int lo = pc.c * CE;
     const int n = min(CE, V - lo);
     const RowPrm P = prm_of(row);
     const int ls = row - row0;
     SliceSlot* sl = &slots[ls % ST_NSLOT];
-    // History pairs of the chunk's segments (absolute offsets into the pair arrays).
-    int p0 = 0, p1 = 0;
-    if (P.mode == ITEM_SAMPLE && a.use_hist) {
-      const int32_t* so = a.seg2 + (int64_t)row * (a.nseg + 1);
-      p0 = so[lo / SEGV];
-      p1 = so[min(a.nseg, (lo + n + SEGV - 1) / SEGV)];
-    }
+    int nn0, nn1, idn[PF];
+    offs_of(g + 2 * ST_NW, p2, nn0, nn1);
+    ids_of(n0, n1, idn);
     if (!warp_mbar_wait(&wbar[s], par)) {
       if (lane == 0) {
         atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
@@ -274,35 +354,74 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
       }
     }
     unsigned char* st = wst + s * ST_CB;
-    bool wrote = false;
-    if (P.mode != ITEM_SKIP) {
+    if (P.mode == ITEM_SKIP) {
+      release(g, pr, s, false);
+    } else {
+      bool wrote = false;
       const char* src = reinterpret_cast<const char*>(a.logits) + ((int64_t)row * a.row_stride + lo) * ES;
       const int nb = (reinterpret_cast<uintptr_t>(src) & 15) == 0 ? ((n * ES) & ~15) : 0;
-      // What the bulk copy skipped (a misaligned chunk, a ragged tail), and -inf padding.
-      for (int e = nb / ES + lane; e < n; e += 32) {
-        copy_elem(st, e, src);
-        wrote = true;
-      }
-      for (int e = n + lane; e < CE; e += 32) {
-        set_neg_inf(st, e);
-        wrote = true;
-      }
-      if (p1 > p0) {
+      // What the bulk copy skipped (a misaligned chunk, a ragged tail) and -inf padding: the only
+      // generic writes into a stage (a row's last chunk, or a row that starts misaligned).
+      if (nb < ST_CB) {
+        for (int e = nb / ES + lane; e < n; e += 32) {
+          copy_elem(st, e, src);
+          wrote = true;
+        }
+        for (int e = n + lane; e < CE; e += 32) {
+          set_neg_inf(st, e);
+          wrote = true;
+        }
         __syncwarp();
-        for (int e = p0 + lane; e < p1; e += 32) {
+      }
+      // History positions of the chunk: the raw value goes to hraw (the resolve kernel applies
+      // the penalties), and a bit in the warp's exclusion map keeps it out of this pass.
+      const bool hp = c1 > c0;
+      if (hp) {
+#pragma unroll
+        for (int k = 0; k < PF; ++k) {
+          if (c0 + 32 * k >= c1) break;  // uniform: no pair in this round or later ones
+          const int pos = idc[k] - lo;
+          if (c0 + lane + 32 * k < c1 && (unsigned)pos < (unsigned)n) {
+            a.hraw[c0 + lane + 32 * k] = elem(st, pos);
+            atomicOr(&xm[pos >> 5], 1u << (pos & 31));
+          }
+        }
+        for (int e = c0 + 32 * PF + lane; e < c1; e += 32) {
           const int pos = a.uniq_ids[e] - lo;
           if ((unsigned)pos < (unsigned)n) {
             a.hraw[e] = elem(st, pos);
-            set_neg_inf(st, pos);
-            wrote = true;
+            atomicOr(&xm[pos >> 5], 1u << (pos & 31));
           }
         }
+        __syncwarp();
       }
-      __syncwarp();
       const uint4* s16 = reinterpret_cast<const uint4*>(st);
       uint4 rv[NV];
 #pragma unroll
       for (int j = 0; j < NV; ++j) rv[j] = s16[j * 32 + lane];
+      if (hp) {
+        // Lane l holds positions (32 j + l) * VPV + q: their bits sit in word
+        // (32 j + l) * VPV / 32 of the map, VPV bits from ((32 j + l) * VPV) % 32.
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+          const int p0v = (32 * j + lane) * VPV;
+          const uint32_t bits = (xm[p0v >> 5] >> (p0v & 31)) & ((1u << VPV) - 1u);
+          if (bits) exclude(rv[j], bits);
+        }
+        __syncwarp();
+        // Clear the words this chunk set, for the warp's next chunk.
+#pragma unroll
+        for (int k = 0; k < PF; ++k) {
+          if (c0 + 32 * k >= c1) break;
+          const int pos = idc[k] - lo;
+          if (c0 + lane + 32 * k < c1 && (unsigned)pos < (unsigned)n) xm[pos >> 5] = 0u;
+        }
+        for (int e = c0 + 32 * PF + lane; e < c1; e += 32) {
+          const int pos = a.uniq_ids[e] - lo;
+          if ((unsigned)pos < (unsigned)n) xm[pos >> 5] = 0u;
+        }
+        __syncwarp();
+      }
       if (P.mode == ITEM_GREEDY) {
         // Greedy row (sampling.py:132-133): argmax of the raw chunk, NaN first, lowest index.
         uint64_t best = 0;
@@ -316,23 +435,36 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
             if (ix + q < lo + n) best = max(best, argmax_code(x[q], ix + q));
         }
         best = wred(best, MaxU64());
+        release(g, pr, s, wrote);  // every value has been read (the reduction consumed them)
         if (lane == 0) atomicMax(&sl->best, (unsigned long long)best);
       } else {
-        float tmax = -INFINITY;
+        // Max as a tree (short dependency chains): per vector, then across the vectors; the
+        // per-vector maxima are kept to skip vectors without candidates below.
+        float vmx[NV];
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
           float x[VPV];
           widen(rv[j], x);
 #pragma unroll
-          for (int q = 0; q < VPV; ++q) tmax = fmax_nan(tmax, x[q]);
+          for (int w2 = VPV / 2; w2 >= 1; w2 /= 2)
+#pragma unroll
+            for (int q = 0; q < w2; ++q) x[q] = fmax_nan(x[q], x[q + w2]);
+          vmx[j] = x[0];
         }
-        const float cmax = wred(tmax, MaxF());
+        float lm = vmx[0];
+#pragma unroll
+        for (int j = 1; j < NV; ++j) lm = fmax_nan(lm, vmx[j]);
+        const float cmax = wred(lm, MaxF());
         const uint32_t ck = (!(cmax == cmax) || cmax == INFINITY) ? 0xffffffffu : f2key(cmax);
         uint32_t mk = 0;
         if (lane == 0) {
-          const uint32_t old = atomicMax(&sl->maxkey, ck);
-          mk = old > ck ? old : ck;
-          if (mk == 0xffffffffu) atomicOr(&sl->flags, SUM_SPECIAL);
+          // The running max as far as this warp can see it: its own chunk's and what the slot
+          // holds (a value read before other warps' updates land is only smaller, which keeps
+          // every threshold taken from it a lower bound).
+          atomicMax(&sl->maxkey, ck);
+          const uint32_t cur = *reinterpret_cast<volatile uint32_t*>(&sl->maxkey);
+          mk = cur > ck ? cur : ck;
+          if (ck == 0xffffffffu) atomicOr(&sl->flags, SUM_SPECIAL);
         }
         mk = __shfl_sync(0xffffffffu, mk, 0);
         const float M = key2f(mk);
@@ -445,67 +577,62 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
             if (lane == 0 && tau > -INFINITY) atomicMax(&sl->taukey, f2key(tau));
             thr = fmaxf(thr, tau);
           }
-          // ---- candidates: finite z >= thr, into the slice's segment
+          // ---- candidates: finite z >= thr, into the slice's segment.  Each lane marks its
+          // values at or above the threshold in a bit mask, and writes only those, reading the
+          // value back from the stage.
           thr = fmaxf(thr, -FLT_MAX);
-          uint32_t cnt = 0;
-#pragma unroll
-          for (int j = 0; j < NV; ++j) {
-            float x[VPV];
-            widen(rv[j], x);
-#pragma unroll
-            for (int q = 0; q < VPV; ++q) cnt += x[q] >= thr ? 1u : 0u;
-          }
-          uint32_t incl = cnt;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += y;
-          }
-          const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-          if (total) {
-            uint32_t base = 0;
-            if (lane == 0) base = atomicAdd(&sl->count, total);
-            base = __shfl_sync(0xffffffffu, base, 0);
-            if (cnt) {
-              const int jsl = blockIdx.x - cta_of_chunk((int64_t)row * C, N, G);
-              uint64_t* out = a.cand + ((int64_t)row * a.MAXSL + jsl) * ST_SEGCAP;
-              uint32_t pos = base + incl - cnt;
+          const bool mine = lm >= thr;
+          if (__ballot_sync(0xffffffffu, mine)) {
+            MaskT m = 0;
+            if (mine) {
 #pragma unroll
               for (int j = 0; j < NV; ++j) {
-                float x[VPV];
-                widen(rv[j], x);
-                const int ix = lo + (j * 32 + lane) * VPV;
+                if (vmx[j] >= thr) {
+                  float x[VPV];
+                  widen(rv[j], x);
 #pragma unroll
-                for (int q = 0; q < VPV; ++q) {
-                  if (x[q] >= thr) {
-                    if (pos < (uint32_t)ST_SEGCAP)
-                      out[pos] = ((uint64_t)f2key(x[q]) << 32) | (uint32_t)(~(uint32_t)(ix + q));
-                    ++pos;
-                  }
+                  for (int q = 0; q < VPV; ++q)
+                    if (x[q] >= thr) m |= (MaskT)1 << (j * VPV + q);
                 }
               }
             }
+            const uint32_t cnt = (uint32_t)(sizeof(MaskT) == 8 ? __popcll((unsigned long long)m) : __popc((uint32_t)m));
+            uint32_t incl = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+              if (lane >= o) incl += y;
+            }
+            const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+            uint32_t base = 0;
+            if (lane == 0) base = atomicAdd(&sl->count, total);
+            base = __shfl_sync(0xffffffffu, base, 0);
+            uint64_t* out = a.cand + ((int64_t)row * a.MAXSL + P.jsl) * ST_SEGCAP;
+            uint32_t pos = base + incl - cnt;
+            while (m) {
+              const int b = sizeof(MaskT) == 8 ? __ffsll((long long)m) - 1 : __ffs((int)m) - 1;
+              m &= m - 1;
+              const int idx = ((b / VPV) * 32 + lane) * VPV + (b % VPV);
+              if (pos < (uint32_t)ST_SEGCAP)
+                out[pos] = ((uint64_t)f2key(elem(st, idx)) << 32) | (uint32_t)(~(uint32_t)(lo + idx));
+              ++pos;
+            }
           }
         }
+        release(g, pr, s, wrote);  // the stage has been read for the last time
       }
     }
-    // ---- release the stage: generic writes to it precede the next bulk copy into it
-    if (wrote) fence_proxy_async();
-    __syncwarp();
-    if (lane == 0 && g + (int64_t)ST_R * ST_NW < g1) issue(g + (int64_t)ST_R * ST_NW, s);
     // ---- chunk done; the slice's last chunk writes the summary and frees the slot
     uint32_t last = 0;
     if (lane == 0) {
       __threadfence_block();
-      const int64_t rs = (int64_t)row * C;
-      const int nch = (int)(min(g1, rs + C) - max(g0, rs));
-      last = atomicAdd(&sl->done, 1u) == (uint32_t)(nch - 1) ? 1u : 0u;
+      last = atomicAdd(&sl->done, 1u) == (uint32_t)(P.nch - 1) ? 1u : 0u;
     }
     last = __shfl_sync(0xffffffffu, last, 0);
     if (last) {
       __threadfence_block();
       if (lane == 0) {
-        const int jsl = blockIdx.x - cta_of_chunk((int64_t)row * C, N, G);
+        const int jsl = P.jsl;
         const volatile SliceSlot* vs = sl;
         uint4 sm;
         if (P.mode == ITEM_GREEDY) {
@@ -525,6 +652,17 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
         *reinterpret_cast<volatile uint32_t*>(&sl->tag) = (uint32_t)(ls + ST_NSLOT);
       }
     }
+    c0 = n0;
+    c1 = n1;
+    n0 = nn0;
+    n1 = nn1;
+    pc = adv(pc, ST_NW);
+    p2 = adv(p2, ST_NW);
+    pr = adv(pr, ST_NW);
+    s = s + 1 == ST_R ? 0 : s + 1;
+    par ^= s == 0 ? 1u : 0u;
+#pragma unroll
+    for (int k = 0; k < PF; ++k) idc[k] = idn[k];
   }
   // After an early stop: chunks i .. min(nwch, i + ST_R) - 1 were issued and not consumed; wait
   // (bounded) for their copies before the CTA's shared memory is released.  After a normal end
