@@ -167,30 +167,66 @@ struct BlockSync {
 
 // =========================================================================================
 // K0: history kernel — one CTA per row: the (id, count) pairs of the rows whose penalties
-// apply, grouped by segments of TS logits (seg2[row][0 .. S] hold the absolute offsets of each
-// segment's pairs in the pair arrays, so the streaming kernel finds a chunk's pairs directly);
-// a per-row flag for ids outside [0, V) or a bad offset range.  Block 0 clears the workspace
-// status first (no other block writes it).
-// Histories of up to PREP_SMEM_SLOTS / 2 ids take a short path: the ids are requested before
-// the table is cleared, slice counts are taken as new keys enter, and one pass over the list
-// of occupied slots scatters the pairs; longer ones go through prep_row's global table.
+// apply (torch.unique(history, return_counts=True), sampling.py:52), sorted by id and grouped
+// by segments of TS logits: seg2[row][0 .. S] hold the absolute offsets of each segment's pairs
+// in the pair arrays, so that the streaming kernel finds a chunk's pairs directly.  A per-row
+// flag records ids outside [0, V) or a bad offset range.  Block 0 clears the workspace status
+// first (no other block writes it).
+//
+// Histories of up to HIST_FAST ids take the bitmap path, which needs no hashing: every id sets
+// its bit in a shared bitmap of the vocabulary; one warp per segment counts the set bits of its
+// 32 words (the rank of each word's first bit within the segment) and a scan over the segments
+// gives every id its rank among the unique ids; the counts are atomic additions on the ranks,
+// and every set bit writes its pair at its rank, which sorts the pairs by id.  Longer histories
+// go through prep_row's global hash table.
 // =========================================================================================
 constexpr int HIST_NT = 1024;
+constexpr int HIST_FAST = 4096;    // history ids of the bitmap path
+constexpr int HIST_IPT = HIST_FAST / HIST_NT;
 
 struct HistArgs {
   RowArgs r;
-  int S, TS;
+  int S, TS;            // segments per row (TS == 1024 logits each)
   int32_t* seg2;        // [B][S + 1]: absolute pair offsets per segment
+  int32_t* pblk;        // [B][S][8]: per segment {first pair, pairs, first six ids}
   uint32_t* rowflag;    // [B]
   uint32_t* header;     // 64 words
 };
 
-__global__ void __launch_bounds__(HIST_NT) lss_hist_kernel(const HistArgs h) {
-  __shared__ uint32_t sw[PREP_SCRATCH_WORDS];
+// The pair blocks of a row whose pairs are in place (seg2 row `so`, pair ids in uniq_ids): one
+// 8-word block per segment with the index of its first pair, its number of pairs and the ids
+// of its first six pairs, so that the streaming kernel finds a chunk's history positions in
+// the bytes it copies with the chunk.  Whole CTA; the pairs and so[] are visible to it.
+__device__ __forceinline__ void write_pair_blocks(const HistArgs& h, int row, const int32_t* so, bool empty) {
+  const RowArgs& a = h.r;
+  int32_t* blk = h.pblk + (int64_t)row * h.S * 8;
+  for (int t = threadIdx.x; t < h.S * 8; t += blockDim.x) {
+    const int sg = t >> 3, f = t & 7;
+    int v = 0;
+    if (!empty) {
+      const int b0 = so[sg], cnt = so[sg + 1] - so[sg];
+      v = f == 0 ? b0 : f == 1 ? cnt : (f - 2 < cnt ? a.uniq_ids[b0 + f - 2] : 0);
+    }
+    blk[t] = v;
+  }
+}
+
+// Dynamic shared memory of K0 for a vocabulary of V: the bitmap path's arrays, or prep_row's
+// scratch, whichever is larger.
+__host__ __device__ constexpr int hist_bm_words(int V) { return (V + 31) / 32; }
+__host__ __device__ constexpr int hist_smem_bytes(int V) {
+  return ((hist_bm_words(V) * 4 + hist_bm_words(V) * 2 + 15) & ~15) + ((PREP_MAXSEG + 1) * 4) + HIST_FAST * 4 >
+                 PREP_SCRATCH_WORDS * 4
+             ? ((hist_bm_words(V) * 4 + hist_bm_words(V) * 2 + 15) & ~15) + ((PREP_MAXSEG + 1) * 4) + HIST_FAST * 4
+             : PREP_SCRATCH_WORDS * 4;
+}
+
+__global__ void __launch_bounds__(HIST_NT, 1) lss_hist_kernel(const HistArgs h) {
+  extern __shared__ __align__(16) uint32_t sw[];
   const RowArgs& a = h.r;
   const int row = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31;
-  pdl_trigger();  // the scan kernel may launch and start its own set-up
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_trigger();  // the streaming kernel may launch and start its own set-up
   if (row == 0 && tid < 64) h.header[tid] = 0u;
   if (tid == 0) h.rowflag[row] = 0u;
   // Every per-row input is requested at once (one round trip), the history offsets included.
@@ -210,83 +246,62 @@ __global__ void __launch_bounds__(HIST_NT) lss_hist_kernel(const HistArgs h) {
   if (bad_range && tid == 0) atomicOr(o.bad, LSS_FLAG_BAD_HISTORY);  // thread 0 cleared it above
   if (!active || H <= 0) {
     if (tid <= nseg) so[tid] = 0;
+    if (a.use_hist) write_pair_blocks(h, row, so, true);
     return;
   }
-  if (2 * H > PREP_SMEM_SLOTS) {
+  if (H > HIST_FAST) {
     __syncthreads();  // rowflag cleared before prep_row may raise it
     prep_row<HIST_NT>(a, row, true, h.TS, nseg, o, sw, BlockSync(), b);
+    __syncthreads();  // the pairs and so[] of this row are written
+    write_pair_blocks(h, row, so, false);
     return;
   }
-  // ---- short path: at most 2 ids per thread
-  constexpr int U = PREP_SMEM_SLOTS / 2 / HIST_NT;
-  int idv[U];
+  // ---- bitmap path
+  const int V = a.V;
+  const int W = hist_bm_words(V);
+  uint32_t* bm = sw;                                                   // [W] one bit per logit
+  uint16_t* wpre = reinterpret_cast<uint16_t*>(sw + W);                // [W] rank of the word's first bit in its segment
+  uint32_t* segpre = sw + ((W * 4 + W * 2 + 15) & ~15) / 4;            // [nseg + 1] rank of each segment's first id
+  uint32_t* cnt = segpre + PREP_MAXSEG + 1;                            // [HIST_FAST] counts by rank
+  int idv[HIST_IPT];
 #pragma unroll
-  for (int t = 0; t < U; ++t) {
+  for (int t = 0; t < HIST_IPT; ++t) {
     const int j = t * HIST_NT + tid;
-    idv[t] = j < H ? a.hist_ids[b + j] : INT32_MIN;
+    idv[t] = j < H ? a.hist_ids[b + j] : -1;
   }
-  uint32_t* keys = sw;
-  uint32_t* cnts = sw + PREP_SMEM_SLOTS;
-  uint16_t* slist = reinterpret_cast<uint16_t*>(sw + 2 * PREP_SMEM_SLOTS);
-  uint32_t* bcnt = sw + 2 * PREP_SMEM_SLOTS + PREP_SMEM_SLOTS / 4;
-  uint32_t* bfill = bcnt + PREP_MAXSEG + 1;
-  uint32_t* nlist = bfill + PREP_MAXSEG + 1;
-  const uint32_t cap = (uint32_t)next_pow2(2 * H);
-  for (uint32_t s2 = tid; s2 < cap; s2 += HIST_NT) {
-    keys[s2] = EMPTY;
-    cnts[s2] = 0;
-  }
-  if (tid <= PREP_MAXSEG) {
-    bcnt[tid] = 0;
-    bfill[tid] = 0;
-  }
-  if (tid == 0) *nlist = 0;
+  for (int w = tid; w < W; w += HIST_NT) bm[w] = 0u;
+  for (int j = tid; j < H; j += HIST_NT) cnt[j] = 0u;
   __syncthreads();
-  const uint32_t TS = (uint32_t)h.TS;
 #pragma unroll
-  for (int t = 0; t < U; ++t) {
-    if (t * HIST_NT >= H) break;  // warp-uniform
-    int id = idv[t] == INT32_MIN ? -1 : idv[t];
-    if (idv[t] != INT32_MIN && (id < 0 || id >= a.V)) {
+  for (int t = 0; t < HIST_IPT; ++t) {
+    int id = idv[t];
+    if (t * HIST_NT + tid < H && (id < 0 || id >= V)) {
       atomicOr(o.bad, LSS_FLAG_BAD_HISTORY);
       id = -1;
     }
-    // Every lane inserts its own id: merging equal ids across the warp first (match.any)
-    // cost more time than the atomics it saves.
-    bool fresh = false;
-    uint32_t slot = 0;
-    if (id >= 0) {
-      uint32_t hh = ((uint32_t)id * 2654435761u) & (cap - 1);
-      for (uint32_t probe = 0; probe < cap; ++probe) {
-        const uint32_t old = atomicCAS(&keys[hh], EMPTY, (uint32_t)id);
-        if (old == EMPTY || old == (uint32_t)id) {
-          atomicAdd(&cnts[hh], 1u);
-          fresh = old == EMPTY;
-          slot = hh;
-          break;
-        }
-        hh = (hh + 1) & (cap - 1);
-      }
+    idv[t] = id;
+    if (id >= 0) atomicOr(&bm[id >> 5], 1u << (id & 31));
+  }
+  __syncthreads();
+  // One warp per segment of 32 words: each word's rank within the segment, the segment total.
+  for (int sgi = warp; sgi < nseg; sgi += HIST_NT / 32) {
+    const int w = sgi * 32 + lane;
+    const uint32_t c = w < W ? (uint32_t)__popc(bm[w]) : 0u;
+    uint32_t incl = c;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += y;
     }
-    const uint32_t bal = __ballot_sync(0xffffffffu, fresh);
-    if (bal) {
-      const int leader = __ffs(bal) - 1;
-      uint32_t base = 0;
-      if (lane == leader) base = atomicAdd(nlist, (uint32_t)__popc(bal));
-      base = __shfl_sync(0xffffffffu, base, leader);
-      if (fresh) {
-        slist[base + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)slot;
-        atomicAdd(&bcnt[(uint32_t)id / TS], 1u);
-      }
-    }
+    if (w < W) wpre[w] = (uint16_t)(incl - c);
+    if (lane == 31) segpre[sgi] = incl;
   }
   __syncthreads();
   {
-    // Exclusive scan of the segment counts (thread c holds segment c; nseg <= PREP_MAXSEG <
-    // HIST_NT), written back relative to the row and to seg2 absolute.
+    // Exclusive scan of the segment totals (thread c holds segment c; nseg <= PREP_MAXSEG <
+    // HIST_NT); seg2 gets the absolute offsets, tid == nseg the row's total.
     __shared__ uint32_t wsum[HIST_NT / 32];
-    const int warp = tid >> 5;
-    const uint32_t v = tid < nseg ? bcnt[tid] : 0u;
+    const uint32_t v = tid < nseg ? segpre[tid] : 0u;
     uint32_t incl = v;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
@@ -298,28 +313,45 @@ __global__ void __launch_bounds__(HIST_NT) lss_hist_kernel(const HistArgs h) {
     uint32_t pre = 0;
     for (int q = 0; q < warp; ++q) pre += wsum[q];
     const uint32_t ex = pre + incl - v;
+    __syncthreads();
     if (tid <= nseg) {
-      if (tid < nseg) bcnt[tid] = ex;
-      so[tid] = b + (int32_t)ex;   // tid == nseg: the row's total
+      segpre[tid] = ex;
+      so[tid] = b + (int32_t)ex;
     }
   }
   __syncthreads();
-  const uint32_t L = *nlist;
-  for (uint32_t i0 = 0; i0 < L; i0 += HIST_NT) {  // warp-uniform trip count
-    const uint32_t i = i0 + tid;
-    const uint32_t s2 = i < L ? (uint32_t)slist[i] : 0u;
-    const uint32_t kk = i < L ? keys[s2] : EMPTY;
-    const int c = kk != EMPTY ? (int)(kk / TS) : -1;
-    const unsigned same = __match_any_sync(0xffffffffu, c);
-    const int leader = __ffs(same) - 1;
-    uint32_t base = 0;
-    if (c >= 0 && lane == leader) base = atomicAdd(&bfill[c], (uint32_t)__popc(same));
-    base = __shfl_sync(0xffffffffu, base, leader);
-    if (c >= 0) {
-      const uint32_t pos = bcnt[c] + base + (uint32_t)__popc(same & ((1u << lane) - 1u));
-      a.uniq_ids[b + pos] = (int32_t)kk;
-      a.uniq_cnt[b + pos] = (int32_t)cnts[s2];
+  // Counts by rank.
+#pragma unroll
+  for (int t = 0; t < HIST_IPT; ++t) {
+    const int id = idv[t];
+    if (id >= 0) {
+      const int w = id >> 5;
+      const uint32_t r = segpre[id >> 10] + wpre[w] + (uint32_t)__popc(bm[w] & ((1u << (id & 31)) - 1u));
+      atomicAdd(&cnt[r], 1u);
     }
+  }
+  __syncthreads();
+  // Every set bit writes its pair at its rank (sorted by id), and the first six ids of each
+  // segment go to its pair block as well.
+  for (int w = tid; w < W; w += HIST_NT) {
+    uint32_t bits = bm[w];
+    if (!bits) continue;
+    const int sg = w >> 5;
+    uint32_t r = segpre[sg] + wpre[w];
+    int32_t* blk = h.pblk + ((int64_t)row * nseg + sg) * 8;
+    while (bits) {
+      const int q = __ffs((int)bits) - 1;
+      bits &= bits - 1u;
+      a.uniq_ids[b + r] = w * 32 + q;
+      a.uniq_cnt[b + r] = (int32_t)cnt[r];
+      if (r - segpre[sg] < 6u) blk[2 + r - segpre[sg]] = w * 32 + q;
+      ++r;
+    }
+  }
+  for (int sg = tid; sg < nseg; sg += HIST_NT) {
+    int32_t* blk = h.pblk + ((int64_t)row * nseg + sg) * 8;
+    blk[0] = b + (int32_t)segpre[sg];
+    blk[1] = (int32_t)(segpre[sg + 1] - segpre[sg]);
   }
 }
 

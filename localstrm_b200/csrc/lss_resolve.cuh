@@ -214,7 +214,7 @@ __device__ __forceinline__ int resolve_cta_of_chunk(int64_t x, int64_t N, int G)
   return (int)(c < G - 1 ? c : G - 1);
 }
 
-__global__ void __launch_bounds__(NT, 1) lss_resolve_kernel(const RowArgs a, const GatherArgs g) {
+__global__ void __launch_bounds__(NT, 2) lss_resolve_kernel(const RowArgs a, const GatherArgs g) {
   constexpr int HPT = 4;  // history values kept in registers per thread
   __shared__ uint64_t G[FAST_CAP];
   __shared__ float E[FAST_CAP];

@@ -173,7 +173,7 @@ static Plan make_plan(int B, int V) {
 // logits) and the global hash table for rows with long histories.  row_path sits at a fixed
 // offset.
 struct WsLayout {
-  size_t header, row_path, summ, cand, seg_off, seg2, rowflag, defer_rows, uniq_ids, uniq_cnt, hraw, gkeys,
+  size_t header, row_path, summ, cand, seg_off, seg2, pblk, rowflag, defer_rows, uniq_ids, uniq_cnt, hraw, gkeys,
       gcnts, total;
 };
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -189,6 +189,7 @@ static WsLayout ws_layout(int B, int V, int64_t H) {
   L.cand = o; o = align256(o + 8 * slices * (size_t)ST_SEGCAP);
   L.seg_off = o; o = align256(o + 4 * b * (MAXCL + 1));
   L.seg2 = o; o = align256(o + 4 * b * (size_t)(pl.nseg + 1));
+  L.pblk = o; o = align256(o + 32 * b * (size_t)pl.nseg);
   L.rowflag = o; o = align256(o + 4 * b);
   L.defer_rows = o; o = align256(o + 4 * b);
   L.uniq_ids = o; o = align256(o + 4 * (h + 4));
@@ -456,10 +457,24 @@ int lss_sample_prepare(int B, int V, const float* temperature, const int32_t* to
   h.S = pl.nseg;
   h.TS = SEGV;
   h.seg2 = reinterpret_cast<int32_t*>(ws + L.seg2);
+  h.pblk = reinterpret_cast<int32_t*>(ws + L.pblk);
   h.rowflag = reinterpret_cast<uint32_t*>(ws + L.rowflag);
   h.header = reinterpret_cast<uint32_t*>(ws + L.header);
   // K0 also clears the header (error flags, deferred-row count) for this call.
-  lss_hist_kernel<<<B, HIST_NT, 0, st>>>(h);
+  {
+    static KernelCfg hist_cfg{};
+    const int smem = hist_smem_bytes(V);
+    const int dev = current_device();
+    std::lock_guard<std::mutex> lock(g_cfg_mu);
+    if (hist_cfg.smem[dev] < smem) {
+      if (cudaFuncSetAttribute(lss_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return LSS_ERR_CUDA;
+      }
+      hist_cfg.smem[dev] = smem;
+    }
+  }
+  lss_hist_kernel<<<B, HIST_NT, hist_smem_bytes(V), st>>>(h);
   if (cudaGetLastError() != cudaSuccess) return LSS_ERR_CUDA;
   return LSS_OK;
 }
@@ -501,6 +516,7 @@ static int sample_rows(const void* logits, int dtype, int B, int V, int64_t row_
   sa.top_k = top_k;
   sa.min_p = min_p;
   sa.seg2 = reinterpret_cast<const int32_t*>(ws + L.seg2);
+  sa.pblk = reinterpret_cast<const int32_t*>(ws + L.pblk);
   sa.uniq_ids = reinterpret_cast<const int32_t*>(ws + L.uniq_ids);
   sa.hraw = reinterpret_cast<float*>(ws + L.hraw);
   sa.summ = reinterpret_cast<uint4*>(ws + L.summ);

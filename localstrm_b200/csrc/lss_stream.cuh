@@ -47,8 +47,10 @@ constexpr int ST_SEGCAP = 1024;               // candidate slots per slice
 constexpr int ST_ROWTAB = 64;                 // rows whose parameters a CTA keeps in shared memory
 constexpr int ST_GCAP = 160;                  // largest grid the workspace layout allows for
 constexpr int SEGV = 1024;                    // history segment: K0 groups the pairs per SEGV logits
-constexpr int ST_STAGE_BYTES = ST_NW * ST_R * ST_CB;
-constexpr int ST_XMW = ST_CB / 2 / 32;        // words of a warp's exclusion map (one bit per logit)
+constexpr int ST_PBW = 8;                     // words of a segment's pair block (K0)
+constexpr int ST_NBK = ST_CB / 2 / SEGV;      // pair blocks a chunk may need (2 for 16-bit logits)
+constexpr int ST_SB = ST_CB + ST_NBK * ST_PBW * 4;  // bytes of a stage: the chunk, then its pair blocks
+constexpr int ST_STAGE_BYTES = ST_NW * ST_R * ST_SB;
 
 constexpr int ITEM_SKIP = 1, ITEM_GREEDY = 2, ITEM_SAMPLE = 3;
 // Summary flags: NaN / +inf among the slice's non-history values.
@@ -91,6 +93,7 @@ struct StreamArgs {
   const int32_t* top_k;
   const float* min_p;
   const int32_t* seg2;  // [B][nseg + 1]: absolute offsets of each segment's pairs (K0)
+  const int32_t* pblk;  // [B][nseg][ST_PBW]: per segment {first pair, pairs, first six ids} (K0)
   const int32_t* uniq_ids;
   float* hraw;          // raw logit at each pair's id (same index as uniq_ids)
   uint4* summ;          // [B][MAXSL]: {max key | argmax code lo, argmax code hi, count, flags}
@@ -99,8 +102,7 @@ struct StreamArgs {
 };
 
 __host__ __device__ constexpr int stream_smem_bytes() {
-  return ST_STAGE_BYTES + ST_NSLOT * (int)sizeof(SliceSlot) + ST_NW * ST_R * 8 + ST_ROWTAB * (int)sizeof(RowPrm) + 16 +
-         ST_NW * ST_XMW * 4;
+  return ST_STAGE_BYTES + ST_NSLOT * (int)sizeof(SliceSlot) + ST_NW * ST_R * 8 + ST_ROWTAB * (int)sizeof(RowPrm) + 16;
 }
 
 // Largest CTA index whose range starts at or before chunk x (ranges [c N / G, (c + 1) N / G)).
@@ -150,8 +152,6 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
   // own copies in flight and returns, with the error flag raised.
   volatile uint32_t* abort_w = reinterpret_cast<volatile uint32_t*>(rtab + ST_ROWTAB);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // Per warp: one bit per logit of the current chunk, set for the history positions.
-  uint32_t* xm = reinterpret_cast<uint32_t*>(rtab + ST_ROWTAB) + 4 + warp * ST_XMW;
   const int G = gridDim.x;
   const int64_t N = a.N;
   const int64_t g0 = (int64_t)blockIdx.x * N / G, g1 = (int64_t)(blockIdx.x + 1) * N / G;
@@ -168,7 +168,6 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
       if (row0 + i < a.B) rtab[i] = make_row_prm(a, row0 + i, g0, g1);
     if (tid < ST_NW * ST_R) fence_barrier_init();
     if (tid == 0) *abort_w = 0u;
-    for (int q = tid; q < ST_NW * ST_XMW; q += ST_NT) reinterpret_cast<uint32_t*>(rtab + ST_ROWTAB)[4 + q] = 0u;
   }
   __syncthreads();
   pdl_trigger();  // the resolve kernel may launch; it waits for this grid before reading
@@ -177,7 +176,7 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
     return row - row0 < ST_ROWTAB ? rtab[row - row0] : make_row_prm(a, row, g0, g1);
   };
   uint64_t* wbar = bars + warp * ST_R;
-  unsigned char* wst = smem + (size_t)warp * ST_R * ST_CB;
+  unsigned char* wst = smem + (size_t)warp * ST_R * ST_SB;
   const int64_t gw = g0 + warp;
   // Positions (row, chunk of the row) are carried forward by adding chunks, so that the loop
   // divides only when it crosses into another row.
@@ -204,8 +203,14 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
     const char* src = reinterpret_cast<const char*>(a.logits) + ((int64_t)row * a.row_stride + lo) * ES;
     const int mode = prm_of(row).mode;
     const int nb = (mode != ITEM_SKIP && (reinterpret_cast<uintptr_t>(src) & 15) == 0) ? ((n * ES) & ~15) : 0;
-    mbar_expect_tx(&wbar[s], (uint32_t)nb);
-    if (nb > 0) bulk_g2s(wst + s * ST_CB, src, (uint32_t)nb, &wbar[s]);
+    // The pair blocks of the chunk's segments travel with it (sampled rows with histories).
+    const int seg0 = lo / SEGV;
+    const int nbk = (mode == ITEM_SAMPLE && a.use_hist) ? min(ST_NBK, a.nseg - seg0) : 0;
+    mbar_expect_tx(&wbar[s], (uint32_t)(nb + nbk * ST_PBW * 4));
+    unsigned char* dst = wst + s * ST_SB;
+    if (nb > 0) bulk_g2s(dst, src, (uint32_t)nb, &wbar[s]);
+    if (nbk > 0)
+      bulk_g2s(dst + ST_CB, a.pblk + ((int64_t)row * a.nseg + seg0) * ST_PBW, (uint32_t)(nbk * ST_PBW * 4), &wbar[s]);
   };
   // The first chunks stream in while K0 still runs: they read nothing K0 writes.
   if (lane == 0)
@@ -228,23 +233,6 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
     if (DT == LSS_DTYPE_F32) reinterpret_cast<float*>(st)[i] = reinterpret_cast<const float*>(src)[i];
     else reinterpret_cast<uint16_t*>(st)[i] = reinterpret_cast<const uint16_t*>(src)[i];
   };
-  // Sets the logits of one 16-byte vector whose bit in `bits` is set to -inf.
-  auto exclude = [&](uint4& r, uint32_t bits) {
-    uint32_t w[4] = {r.x, r.y, r.z, r.w};
-    if (DT == LSS_DTYPE_F32) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if ((bits >> q) & 1u) w[q] = 0xff800000u;
-    } else {
-      const uint32_t ni = DT == LSS_DTYPE_BF16 ? 0xff80u : 0xfc00u;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if ((bits >> (2 * q)) & 1u) w[q] = (w[q] & 0xffff0000u) | ni;
-        if ((bits >> (2 * q + 1)) & 1u) w[q] = (w[q] & 0x0000ffffu) | (ni << 16);
-      }
-    }
-    r = make_uint4(w[0], w[1], w[2], w[3]);
-  };
   using MaskT = typename std::conditional<(NV * VPV > 32), unsigned long long, uint32_t>::type;
   // The logits of 16-byte vector q of a stage, widened to f32.
   auto widen = [&](const uint4 r, float* x) {
@@ -266,31 +254,6 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
     }
   };
 
-  // History pairs of chunk gg: absolute offsets [q0, q1) into the pair arrays (K0 grouped them
-  // by SEGV-logit segments, and chunks start on segment boundaries).
-  auto offs_of = [&](int64_t gg, Pos p, int& q0, int& q1) {
-    q0 = q1 = 0;
-    if (gg < g1 && a.use_hist) {
-      const int r = p.row;
-      if (prm_of(r).mode == ITEM_SAMPLE) {
-        const int l0 = p.c * CE;
-        const int nn = min(CE, V - l0);
-        const int32_t* so = a.seg2 + (int64_t)r * (a.nseg + 1);
-        q0 = so[l0 / SEGV];
-        q1 = so[min(a.nseg, (l0 + nn + SEGV - 1) / SEGV)];
-      }
-    }
-  };
-  // The first PF * 32 history ids of a chunk are fetched one chunk ahead, its offsets two chunks
-  // ahead, so that their latency hides behind the chunk before.
-  constexpr int PF = 8;
-  auto ids_of = [&](int q0, int q1, int* idv) {
-#pragma unroll
-    for (int k = 0; k < PF; ++k) {
-      const int e = q0 + lane + 32 * k;
-      idv[k] = e < q1 ? a.uniq_ids[e] : -1;
-    }
-  };
   // Stage s of chunk g is no longer read: generic writes to it precede the next bulk copy into it.
   auto release = [&](int64_t g, Pos pi, int s, bool wrote) {
     if (wrote) fence_proxy_async();
@@ -299,29 +262,22 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
   };
 
   const int nwch = gw < g1 ? (int)((g1 - gw + ST_NW - 1) / ST_NW) : 0;  // this warp's chunks
-  int c0, c1, n0, n1;  // pair offsets of this chunk and of the next one
-  int idc[PF];         // ids of this chunk's first pairs
   Pos pc = pw;                       // this chunk
-  Pos p2 = adv(pw, 2 * ST_NW);        // two chunks on (history offsets)
   Pos pr = adv(pw, ST_R * ST_NW);     // ST_R chunks on (the copy started when this one is released)
-  offs_of(gw, pc, c0, c1);
-  offs_of(gw + ST_NW, adv(pw, ST_NW), n0, n1);
-  ids_of(c0, c1, idc);
   int i = 0;
   int s = 0;
   uint32_t par = 0;
+  int crow = -1;        // row of the slice this warp is in (its parameters and slot below)
+  int mine = 0;         // chunks of that slice this warp has finished
+  RowPrm P{};
+  SliceSlot* sl = slots;
   for (;; ++i) {
     const int64_t g = gw + (int64_t)i * ST_NW;
     if (g >= g1 || __shfl_sync(0xffffffffu, lane == 0 ? *abort_w : 0u, 0)) break;
     const int row = pc.row;
     const int lo = pc.c * CE;
     const int n = min(CE, V - lo);
-    const RowPrm P = prm_of(row);
     const int ls = row - row0;
-    SliceSlot* sl = &slots[ls % ST_NSLOT];
-    int nn0, nn1, idn[PF];
-    offs_of(g + 2 * ST_NW, p2, nn0, nn1);
-    ids_of(n0, n1, idn);
     if (!warp_mbar_wait(&wbar[s], par)) {
       if (lane == 0) {
         atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
@@ -330,8 +286,13 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
       __syncwarp();
       break;
     }
-    // The slot of this slice: free once the slice ST_NSLOT before it has been summarised.  The
-    // whole warp waits in one uniform loop (lane 0 reads and decides, the lanes follow).
+    // Entering a slice: its parameters, and its slot, free once the slice ST_NSLOT before it has
+    // been summarised.  The whole warp waits in one uniform loop (lane 0 reads and decides, the
+    // lanes follow).  The slot stays the slice's until this warp has reported its chunks.
+    if (row != crow) {
+    crow = row;
+    P = prm_of(row);
+    sl = &slots[ls % ST_NSLOT];
     volatile uint32_t* vtag = &sl->tag;
     if (__shfl_sync(0xffffffffu, lane == 0 ? *vtag : 0u, 0) != (uint32_t)ls) {
       const long long t0 = clock64();
@@ -353,7 +314,8 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
         break;
       }
     }
-    unsigned char* st = wst + s * ST_CB;
+    }
+    unsigned char* st = wst + s * ST_SB;
     if (P.mode == ITEM_SKIP) {
       release(g, pr, s, false);
     } else {
@@ -374,23 +336,42 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
         __syncwarp();
       }
       // History positions of the chunk: the raw value goes to hraw (the resolve kernel applies
-      // the penalties), and a bit in the warp's exclusion map keeps it out of this pass.
-      const bool hp = c1 > c0;
-      if (hp) {
-#pragma unroll
-        for (int k = 0; k < PF; ++k) {
-          if (c0 + 32 * k >= c1) break;  // uniform: no pair in this round or later ones
-          const int pos = idc[k] - lo;
-          if (c0 + lane + 32 * k < c1 && (unsigned)pos < (unsigned)n) {
-            a.hraw[c0 + lane + 32 * k] = elem(st, pos);
-            atomicOr(&xm[pos >> 5], 1u << (pos & 31));
+      // the penalties) and the stage holds -inf in its place.  The chunk's pair blocks (one per
+      // segment) arrived with it: the first pair's index, the number of pairs, the first six
+      // ids; further ids of a segment come from the pair array.
+      if (P.mode == ITEM_SAMPLE && a.use_hist) {
+        const int32_t* blk = reinterpret_cast<const int32_t*>(st + ST_CB);
+        const int nbk = min(ST_NBK, a.nseg - lo / SEGV);
+        for (int sb = 0; sb < nbk; ++sb) {
+          const int base = blk[sb * ST_PBW], cnt = blk[sb * ST_PBW + 1];
+          if (cnt <= 0) continue;
+          if (lane < min(cnt, ST_PBW - 2)) {
+            const int pos = blk[sb * ST_PBW + 2 + lane] - lo;
+            if ((unsigned)pos < (unsigned)n) {
+              a.hraw[base + lane] = elem(st, pos);
+              set_neg_inf(st, pos);
+              wrote = true;
+            }
           }
-        }
-        for (int e = c0 + 32 * PF + lane; e < c1; e += 32) {
-          const int pos = a.uniq_ids[e] - lo;
-          if ((unsigned)pos < (unsigned)n) {
-            a.hraw[e] = elem(st, pos);
-            atomicOr(&xm[pos >> 5], 1u << (pos & 31));
+          // Further ids: eight per lane requested at once, so that a segment with hundreds of
+          // pairs (a row's first chunk) costs one or two round trips.
+          for (int e0 = ST_PBW - 2; e0 < cnt; e0 += 32 * 8) {
+            int idv[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int e = e0 + 32 * k + lane;
+              idv[k] = e < cnt ? a.uniq_ids[base + e] : -1;
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int e = e0 + 32 * k + lane;
+              const int pos = idv[k] - lo;
+              if (e < cnt && (unsigned)pos < (unsigned)n) {
+                a.hraw[base + e] = elem(st, pos);
+                set_neg_inf(st, pos);
+                wrote = true;
+              }
+            }
           }
         }
         __syncwarp();
@@ -399,29 +380,6 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
       uint4 rv[NV];
 #pragma unroll
       for (int j = 0; j < NV; ++j) rv[j] = s16[j * 32 + lane];
-      if (hp) {
-        // Lane l holds positions (32 j + l) * VPV + q: their bits sit in word
-        // (32 j + l) * VPV / 32 of the map, VPV bits from ((32 j + l) * VPV) % 32.
-#pragma unroll
-        for (int j = 0; j < NV; ++j) {
-          const int p0v = (32 * j + lane) * VPV;
-          const uint32_t bits = (xm[p0v >> 5] >> (p0v & 31)) & ((1u << VPV) - 1u);
-          if (bits) exclude(rv[j], bits);
-        }
-        __syncwarp();
-        // Clear the words this chunk set, for the warp's next chunk.
-#pragma unroll
-        for (int k = 0; k < PF; ++k) {
-          if (c0 + 32 * k >= c1) break;
-          const int pos = idc[k] - lo;
-          if (c0 + lane + 32 * k < c1 && (unsigned)pos < (unsigned)n) xm[pos >> 5] = 0u;
-        }
-        for (int e = c0 + 32 * PF + lane; e < c1; e += 32) {
-          const int pos = a.uniq_ids[e] - lo;
-          if ((unsigned)pos < (unsigned)n) xm[pos >> 5] = 0u;
-        }
-        __syncwarp();
-      }
       if (P.mode == ITEM_GREEDY) {
         // Greedy row (sampling.py:132-133): argmax of the raw chunk, NaN first, lowest index.
         uint64_t best = 0;
@@ -622,13 +580,19 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
         release(g, pr, s, wrote);  // the stage has been read for the last time
       }
     }
-    // ---- chunk done; the slice's last chunk writes the summary and frees the slot
+    // ---- chunk done.  A warp leaving a slice reports its chunks of it at once; the report
+    // that completes the slice writes the summary and frees the slot.
+    ++mine;
+    const Pos pnext = adv(pc, ST_NW);
     uint32_t last = 0;
-    if (lane == 0) {
-      __threadfence_block();
-      last = atomicAdd(&sl->done, 1u) == (uint32_t)(P.nch - 1) ? 1u : 0u;
+    if (g + ST_NW >= g1 || pnext.row != row) {
+      if (lane == 0) {
+        __threadfence_block();
+        last = atomicAdd(&sl->done, (uint32_t)mine) + (uint32_t)mine == (uint32_t)P.nch ? 1u : 0u;
+      }
+      mine = 0;
+      last = __shfl_sync(0xffffffffu, last, 0);
     }
-    last = __shfl_sync(0xffffffffu, last, 0);
     if (last) {
       __threadfence_block();
       if (lane == 0) {
@@ -652,17 +616,12 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
         *reinterpret_cast<volatile uint32_t*>(&sl->tag) = (uint32_t)(ls + ST_NSLOT);
       }
     }
-    c0 = n0;
-    c1 = n1;
-    n0 = nn0;
-    n1 = nn1;
-    pc = adv(pc, ST_NW);
-    p2 = adv(p2, ST_NW);
+
+    pc = pnext;
+
     pr = adv(pr, ST_NW);
     s = s + 1 == ST_R ? 0 : s + 1;
     par ^= s == 0 ? 1u : 0u;
-#pragma unroll
-    for (int k = 0; k < PF; ++k) idc[k] = idn[k];
   }
   // After an early stop: chunks i .. min(nwch, i + ST_R) - 1 were issued and not consumed; wait
   // (bounded) for their copies before the CTA's shared memory is released.  After a normal end
