@@ -3,8 +3,8 @@
 Workload (the metric point): B=256 rows per GPU, V=151,936, float32 logits with config 3's
 distribution (Gumbel background + Zipf-ranked head) and parameters (T 0.7, top-p 0.95,
 min-p 0.05, repetition 1.1, frequency 0.3, presence 0.2, 2,048-id histories), seeded per rank.
-A step is one ``lss_sample`` over the batch (K0 history pairs, K1 streaming pass, K2 per-row
-resolve, K3 dense rows), replayed as one CUDA graph.  With N GPUs (one process per GPU) each
+A step is one ``lss_sample`` over the batch (K1 streaming pass, K2 per-row history pairs and
+resolve, K3 deferred rows), replayed as one CUDA graph.  With N GPUs (one process per GPU) each
 rank samples its own rows and every step ends with the row mode's exchange, one NCCL
 all-gather of the int32 token ids, inside the timed region; the time is the maximum over
 ranks.  By default every rank has its own 256 rows (weak scaling); ``--strong`` splits the
@@ -353,7 +353,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         gather()
     torch.cuda.synchronize()
 
-    # One CUDA graph per input buffer: a step (prepare + rows: four kernels chained by
+    # One CUDA graph per input buffer: a step (prepare + rows: three kernels chained by
     # programmatic dependent launch) is one graph launch, as a decode loop would replay it.
     graphs, scan_graphs = [], []
     for i in range(NBUF):
@@ -507,7 +507,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                          "algorithmic_bytes_per_launch": alg, "kernel_ms": kern_avg_ms},
             "step_ms_median": statistics.median(step_ms_each),
             "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
-            "gpu_launches": 4 * n_steps_total,
+            "gpu_launches": 3 * n_steps_total,
             "row_paths": {str(k): int((paths == k).sum()) for k in np.unique(paths)},
             "device_flags": flags,
         }

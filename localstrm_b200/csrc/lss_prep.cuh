@@ -5,9 +5,8 @@
 // in the shared memory handed in (and the slots they occupy are listed, so that grouping
 // walks only those), longer ones in a global table of 2H slots.  The pairs of
 // slice c ([c*TE, (c+1)*TE)) land in uniq_ids / uniq_cnt[hist_off[row] + so[c] ..
-// hist_off[row] + so[c+1]).  K0, lss_hist_kernel, runs it for every row with the scan
-// kernel's slices; the second kernel runs it again for the rows it takes, with its own
-// slices.
+// hist_off[row] + so[c+1]).  The second kernel runs it for the rows it takes, with its own
+// slices (the resolve kernel keeps the pairs of the other rows in its own shared memory).
 #pragma once
 
 #include "lss_common.cuh"
@@ -164,195 +163,5 @@ __device__ void prep_row(const RowArgs& a, int row, bool active, int TE, int nse
 struct BlockSync {
   __device__ void operator()() const { __syncthreads(); }
 };
-
-// =========================================================================================
-// K0: history kernel — one CTA per row: the (id, count) pairs of the rows whose penalties
-// apply (torch.unique(history, return_counts=True), sampling.py:52), sorted by id and grouped
-// by segments of TS logits: seg2[row][0 .. S] hold the absolute offsets of each segment's pairs
-// in the pair arrays, so that the streaming kernel finds a chunk's pairs directly.  A per-row
-// flag records ids outside [0, V) or a bad offset range.  Block 0 clears the workspace status
-// first (no other block writes it).
-//
-// Histories of up to HIST_FAST ids take the bitmap path, which needs no hashing: every id sets
-// its bit in a shared bitmap of the vocabulary; one warp per segment counts the set bits of its
-// 32 words (the rank of each word's first bit within the segment) and a scan over the segments
-// gives every id its rank among the unique ids; the counts are atomic additions on the ranks,
-// and every set bit writes its pair at its rank, which sorts the pairs by id.  Longer histories
-// go through prep_row's global hash table.
-// =========================================================================================
-constexpr int HIST_NT = 1024;
-constexpr int HIST_FAST = 4096;    // history ids of the bitmap path
-constexpr int HIST_IPT = HIST_FAST / HIST_NT;
-
-struct HistArgs {
-  RowArgs r;
-  int S, TS;            // segments per row (TS == 1024 logits each)
-  int32_t* seg2;        // [B][S + 1]: absolute pair offsets per segment
-  int32_t* pblk;        // [B][S][8]: per segment {first pair, pairs, first six ids}
-  uint32_t* rowflag;    // [B]
-  uint32_t* header;     // 64 words
-};
-
-// The pair blocks of a row whose pairs are in place (seg2 row `so`, pair ids in uniq_ids): one
-// 8-word block per segment with the index of its first pair, its number of pairs and the ids
-// of its first six pairs, so that the streaming kernel finds a chunk's history positions in
-// the bytes it copies with the chunk.  Whole CTA; the pairs and so[] are visible to it.
-__device__ __forceinline__ void write_pair_blocks(const HistArgs& h, int row, const int32_t* so, bool empty) {
-  const RowArgs& a = h.r;
-  int32_t* blk = h.pblk + (int64_t)row * h.S * 8;
-  for (int t = threadIdx.x; t < h.S * 8; t += blockDim.x) {
-    const int sg = t >> 3, f = t & 7;
-    int v = 0;
-    if (!empty) {
-      const int b0 = so[sg], cnt = so[sg + 1] - so[sg];
-      v = f == 0 ? b0 : f == 1 ? cnt : (f - 2 < cnt ? a.uniq_ids[b0 + f - 2] : 0);
-    }
-    blk[t] = v;
-  }
-}
-
-// Dynamic shared memory of K0 for a vocabulary of V: the bitmap path's arrays, or prep_row's
-// scratch, whichever is larger.
-__host__ __device__ constexpr int hist_bm_words(int V) { return (V + 31) / 32; }
-__host__ __device__ constexpr int hist_smem_bytes(int V) {
-  return ((hist_bm_words(V) * 4 + hist_bm_words(V) * 2 + 15) & ~15) + ((PREP_MAXSEG + 1) * 4) + HIST_FAST * 4 >
-                 PREP_SCRATCH_WORDS * 4
-             ? ((hist_bm_words(V) * 4 + hist_bm_words(V) * 2 + 15) & ~15) + ((PREP_MAXSEG + 1) * 4) + HIST_FAST * 4
-             : PREP_SCRATCH_WORDS * 4;
-}
-
-__global__ void __launch_bounds__(HIST_NT, 1) lss_hist_kernel(const HistArgs h) {
-  extern __shared__ __align__(16) uint32_t sw[];
-  const RowArgs& a = h.r;
-  const int row = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  pdl_trigger();  // the streaming kernel may launch and start its own set-up
-  if (row == 0 && tid < 64) h.header[tid] = 0u;
-  if (tid == 0) h.rowflag[row] = 0u;
-  // Every per-row input is requested at once (one round trip), the history offsets included.
-  const float T = a.temperature[row];
-  const int k = a.top_k[row];
-  const float mp = a.min_p[row];
-  const float rp = a.rep[row], fq = a.freq[row], pr = a.pres[row];
-  int b = 0, e = 0;
-  bool bad_range = false;
-  if (a.use_hist) bad_range = !hist_range(a.hist_off, row, a.H, b, e);
-  const bool bounded = (k > 0 && k < a.V) || (mp > 0.0f && mp < 1.0f) || a.V <= FAST_CAP / 2;
-  const bool active = a.use_hist && T > 0.0f && bounded && (rp != 1.0f || fq != 0.0f || pr != 0.0f);
-  const int nseg = h.S;
-  int32_t* so = h.seg2 + (int64_t)row * (nseg + 1);
-  const PrepOut o{so, h.rowflag + row};
-  const int H = active ? e - b : 0;
-  if (bad_range && tid == 0) atomicOr(o.bad, LSS_FLAG_BAD_HISTORY);  // thread 0 cleared it above
-  if (!active || H <= 0) {
-    if (tid <= nseg) so[tid] = 0;
-    if (a.use_hist) write_pair_blocks(h, row, so, true);
-    return;
-  }
-  if (H > HIST_FAST) {
-    __syncthreads();  // rowflag cleared before prep_row may raise it
-    prep_row<HIST_NT>(a, row, true, h.TS, nseg, o, sw, BlockSync(), b);
-    __syncthreads();  // the pairs and so[] of this row are written
-    write_pair_blocks(h, row, so, false);
-    return;
-  }
-  // ---- bitmap path
-  const int V = a.V;
-  const int W = hist_bm_words(V);
-  uint32_t* bm = sw;                                                   // [W] one bit per logit
-  uint16_t* wpre = reinterpret_cast<uint16_t*>(sw + W);                // [W] rank of the word's first bit in its segment
-  uint32_t* segpre = sw + ((W * 4 + W * 2 + 15) & ~15) / 4;            // [nseg + 1] rank of each segment's first id
-  uint32_t* cnt = segpre + PREP_MAXSEG + 1;                            // [HIST_FAST] counts by rank
-  int idv[HIST_IPT];
-#pragma unroll
-  for (int t = 0; t < HIST_IPT; ++t) {
-    const int j = t * HIST_NT + tid;
-    idv[t] = j < H ? a.hist_ids[b + j] : -1;
-  }
-  for (int w = tid; w < W; w += HIST_NT) bm[w] = 0u;
-  for (int j = tid; j < H; j += HIST_NT) cnt[j] = 0u;
-  __syncthreads();
-#pragma unroll
-  for (int t = 0; t < HIST_IPT; ++t) {
-    int id = idv[t];
-    if (t * HIST_NT + tid < H && (id < 0 || id >= V)) {
-      atomicOr(o.bad, LSS_FLAG_BAD_HISTORY);
-      id = -1;
-    }
-    idv[t] = id;
-    if (id >= 0) atomicOr(&bm[id >> 5], 1u << (id & 31));
-  }
-  __syncthreads();
-  // One warp per segment of 32 words: each word's rank within the segment, the segment total.
-  for (int sgi = warp; sgi < nseg; sgi += HIST_NT / 32) {
-    const int w = sgi * 32 + lane;
-    const uint32_t c = w < W ? (uint32_t)__popc(bm[w]) : 0u;
-    uint32_t incl = c;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, d);
-      if (lane >= d) incl += y;
-    }
-    if (w < W) wpre[w] = (uint16_t)(incl - c);
-    if (lane == 31) segpre[sgi] = incl;
-  }
-  __syncthreads();
-  {
-    // Exclusive scan of the segment totals (thread c holds segment c; nseg <= PREP_MAXSEG <
-    // HIST_NT); seg2 gets the absolute offsets, tid == nseg the row's total.
-    __shared__ uint32_t wsum[HIST_NT / 32];
-    const uint32_t v = tid < nseg ? segpre[tid] : 0u;
-    uint32_t incl = v;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, d);
-      if (lane >= d) incl += y;
-    }
-    if (lane == 31) wsum[warp] = incl;
-    __syncthreads();
-    uint32_t pre = 0;
-    for (int q = 0; q < warp; ++q) pre += wsum[q];
-    const uint32_t ex = pre + incl - v;
-    __syncthreads();
-    if (tid <= nseg) {
-      segpre[tid] = ex;
-      so[tid] = b + (int32_t)ex;
-    }
-  }
-  __syncthreads();
-  // Counts by rank.
-#pragma unroll
-  for (int t = 0; t < HIST_IPT; ++t) {
-    const int id = idv[t];
-    if (id >= 0) {
-      const int w = id >> 5;
-      const uint32_t r = segpre[id >> 10] + wpre[w] + (uint32_t)__popc(bm[w] & ((1u << (id & 31)) - 1u));
-      atomicAdd(&cnt[r], 1u);
-    }
-  }
-  __syncthreads();
-  // Every set bit writes its pair at its rank (sorted by id), and the first six ids of each
-  // segment go to its pair block as well.
-  for (int w = tid; w < W; w += HIST_NT) {
-    uint32_t bits = bm[w];
-    if (!bits) continue;
-    const int sg = w >> 5;
-    uint32_t r = segpre[sg] + wpre[w];
-    int32_t* blk = h.pblk + ((int64_t)row * nseg + sg) * 8;
-    while (bits) {
-      const int q = __ffs((int)bits) - 1;
-      bits &= bits - 1u;
-      a.uniq_ids[b + r] = w * 32 + q;
-      a.uniq_cnt[b + r] = (int32_t)cnt[r];
-      if (r - segpre[sg] < 6u) blk[2 + r - segpre[sg]] = w * 32 + q;
-      ++r;
-    }
-  }
-  for (int sg = tid; sg < nseg; sg += HIST_NT) {
-    int32_t* blk = h.pblk + ((int64_t)row * nseg + sg) * 8;
-    blk[0] = b + (int32_t)segpre[sg];
-    blk[1] = (int32_t)(segpre[sg + 1] - segpre[sg]);
-  }
-}
 
 }  // namespace lss

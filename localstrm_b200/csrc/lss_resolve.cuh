@@ -34,15 +34,18 @@ struct RedScratch {
 
 // Whole-CTA resolve of G[0, nc) (nc <= cap, cap a power of two >= NT * per-thread items).
 // E must hold `cap` floats.  Writes the token and, when requested, kept/probs.
+// `presorted`: G[0, nc) is already in that order.
 template <int CAPN>
 __device__ void resolve_block(uint64_t* G, float* E, int nc, const ResolveIn& in, const RowArgs& a,
-                              const RedScratch& rs, int path) {
+                              const RedScratch& rs, int path, bool presorted = false) {
   constexpr int PER = CAPN / NT;  // items per thread, contiguous
   const int tid = threadIdx.x;
-  const int np = next_pow2(nc > 1 ? nc : 1);
-  for (int i = nc + tid; i < np; i += NT) G[i] = 0ull;
-  __syncthreads();
-  bitonic_sort(G, np, true);  // key desc, index asc
+  if (!presorted) {
+    const int np = next_pow2(nc > 1 ? nc : 1);
+    for (int i = nc + tid; i < np; i += NT) G[i] = 0ull;
+    __syncthreads();
+    bitonic_sort(G, np, true);  // key desc, index asc
+  }
   int n1 = nc;
   if (in.tk && in.k <= nc) {  // top-k keeps every value >= the k-th largest (sampling.py:85)
     const uint32_t Kk = (uint32_t)(G[in.k - 1] >> 32);
@@ -186,27 +189,42 @@ __device__ void resolve_warp(uint64_t v, int nc, const ResolveIn& in, const RowA
 // =========================================================================================
 // K2: resolve kernel — one CTA per row.
 //
-// Greedy rows: the largest argmax code of the row's slices.  Sampled rows: the exact row max
-// of z over the slices' maxima of the non-history values and over the history values, whose
-// penalties are applied here from the raw logits the streaming kernel set aside
-// (sampling.py:52-66: x > 0 ? x / rep : x * rep, then x - (freq * count + pres)); y = z / T
-// (sampling.py:146); every candidate and every history value divided exactly and kept when y
-// is finite and at or above the exact min-p key (sampling.py:89-94), then the sort / top-k /
-// top-p / draw of resolve_warp or resolve_block.  Rows that need the whole vocabulary (top-p
-// only or no filter on a large vocabulary), rows with NaN / +inf / only -inf after scaling
-// (the NaN guard, sampling.py:159-160), and rows whose candidates overflow the fixed buffers go
-// to the deferred list for the second kernel.
+// Greedy rows: the largest argmax code of the row's slices.  Sampled rows:
+//   * before it waits for the streaming kernel (inputs only): the history as unique (id, count)
+//     pairs in a shared hash table (torch.unique(..., return_counts=True), sampling.py:52), the
+//     raw logit at each id read from the logits, and the penalties applied (sampling.py:55-66:
+//     x > 0 ? x / rep : x * rep, then x - (freq * count + pres));
+//   * the exact row max of z over the candidates that are not history ids and over the
+//     penalised history values; y = z / T (sampling.py:146); every such value kept when y is
+//     finite and at or above the exact min-p key (sampling.py:89-94);
+//   * the check that makes the candidates exact: every value of a slice that is not a
+//     candidate lies below the slice's largest threshold U (streaming kernel), so once the
+//     cut (min-p key, and the k-th largest kept value for top-k rows) lies above every U / T,
+//     nothing outside the candidates can survive.  A slice whose U / T reaches the cut (a
+//     history value counted there with its raw value raised its threshold) is re-read from the
+//     logits for every value at or above the cut, and the cut is taken again;
+//   * then the sort / top-k / top-p / draw of resolve_warp or resolve_block.
+// Rows that need the whole vocabulary (top-p only or no filter on a large vocabulary), rows with
+// NaN / +inf / only -inf after scaling (the NaN guard, sampling.py:159-160), rows with more
+// than RH_CAP history ids, and rows whose candidates overflow the fixed buffers go to the
+// deferred list for the second kernel.
 // =========================================================================================
+constexpr int RH_CAP = 2048;          // history ids of a row this kernel takes
+constexpr int RH_SLOTS = 2 * RH_CAP;  // its shared hash table (load <= 1/2)
+
 struct GatherArgs {
-  const uint4* summ;        // [B][MAXSL]
+  const uint4* summ;        // [B][MAXSL]: {max key | argmax lo, threshold key | argmax hi, count, flags}
   const uint64_t* cand;     // [B][MAXSL][SEGCAP]
   int MAXSL, SEGCAP, C, G;  // slice stride, segment capacity, chunks per row, streaming grid
   int64_t N;                // chunks in all
-  int nseg;                 // history segments per row
-  const int32_t* seg2;      // [B][nseg + 1] absolute pair offsets (K0)
-  const float* hraw;        // raw logit at each pair's id (streaming kernel)
-  const uint32_t* rowflag;  // [B] history flags of K0
+  int CE;                   // logits per chunk
+  int dtype;                // LSS_DTYPE_* of the logits
+  const uint32_t* cmax;     // [B * C]: key of each sampled chunk's max (streaming kernel)
 };
+
+// Dynamic shared memory of K2: hash keys and counts, the penalised value and the slot of each
+// listed pair.
+__host__ __device__ constexpr int resolve_smem_bytes() { return RH_SLOTS * 8 + RH_CAP * 4 + RH_CAP * 2; }
 
 // Largest CTA index whose chunk range [c N / G, (c + 1) N / G) starts at or before chunk x.
 __device__ __forceinline__ int resolve_cta_of_chunk(int64_t x, int64_t N, int G) {
@@ -214,8 +232,21 @@ __device__ __forceinline__ int resolve_cta_of_chunk(int64_t x, int64_t N, int G)
   return (int)(c < G - 1 ? c : G - 1);
 }
 
+__device__ __forceinline__ float load_logit(const void* base, int dtype, int64_t i) {
+  if (dtype == LSS_DTYPE_F32) return reinterpret_cast<const float*>(base)[i];
+  const uint16_t h = reinterpret_cast<const uint16_t*>(base)[i];
+  if (dtype == LSS_DTYPE_BF16) return __uint_as_float((uint32_t)h << 16);
+  return __half2float(__ushort_as_half(h));
+}
+
 __global__ void __launch_bounds__(NT, 2) lss_resolve_kernel(const RowArgs a, const GatherArgs g) {
-  constexpr int HPT = 4;  // history values kept in registers per thread
+  constexpr int HPT = RH_CAP / NT;  // history ids per thread
+  constexpr int PER = FAST_CAP / NT;
+  extern __shared__ __align__(16) uint32_t rsm[];
+  uint32_t* hkeys = rsm;
+  uint32_t* hcnts = rsm + RH_SLOTS;
+  float* hz = reinterpret_cast<float*>(rsm + 2 * RH_SLOTS);
+  uint16_t* hslot = reinterpret_cast<uint16_t*>(hz + RH_CAP);
   __shared__ uint64_t G[FAST_CAP];
   __shared__ float E[FAST_CAP];
   __shared__ uint64_t r64[NWARP];
@@ -225,11 +256,12 @@ __global__ void __launch_bounds__(NT, 2) lss_resolve_kernel(const RowArgs a, con
   __shared__ float rf[NWARP];
   __shared__ uint32_t s_pre[NT + 1];
   __shared__ uint32_t s_cnt[NT];
-  __shared__ uint32_t s_n, s_kmp;
+  __shared__ uint32_t s_uy[NT];
+  __shared__ uint32_t s_n, s_kmp, s_nh, s_hflags;
   __shared__ int s_defer;
   __shared__ float s_my;
   const int row = blockIdx.x;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
   const int V = a.V;
   const float T = a.temperature[row];
   const int k = a.top_k[row];
@@ -241,11 +273,105 @@ __global__ void __launch_bounds__(NT, 2) lss_resolve_kernel(const RowArgs a, con
   const bool bounded = greedy || tk_on || mp_on || V <= FAST_CAP / 2;
   const int cf = resolve_cta_of_chunk((int64_t)row * g.C, g.N, g.G);
   const int cl = resolve_cta_of_chunk((int64_t)(row + 1) * g.C - 1, g.N, g.G);
-  const int nsl = cl - cf + 1;  // slices of this row (<= MAXSL)
+  const int nsl = cl - cf + 1;  // slices of this row (<= MAXSL <= NT)
   const RedScratch rs{r64, rd, r32, ri};
+  const char* zrow = reinterpret_cast<const char*>(a.logits) +
+                     (int64_t)row * a.row_stride * (g.dtype == LSS_DTYPE_F32 ? 4 : 2);
+
+  // ---- history (inputs only: runs while the streaming kernel may still be busy elsewhere)
+  const bool hist_on = a.use_hist && !greedy && bounded && (rp != 1.0f || fq != 0.0f || pr != 0.0f);
+  int hb = 0, he = 0;
+  const bool bad_range = hist_on && !hist_range(a.hist_off, row, a.H, hb, he);
+  const int H = he - hb;
+  const bool hist_long = H > RH_CAP;
+  const uint32_t cap = (H > 0 && !hist_long) ? (uint32_t)next_pow2(max(2 * H, 64)) : 0u;
+  if (tid == 0) {
+    s_nh = 0u;
+    s_hflags = bad_range ? LSS_FLAG_BAD_HISTORY : 0u;
+  }
+  float hmax = -INFINITY;
+  bool hspecial = false;
+  if (cap) {
+    int idv[HPT];
+#pragma unroll
+    for (int t = 0; t < HPT; ++t) {
+      const int j = t * NT + tid;
+      idv[t] = j < H ? a.hist_ids[hb + j] : INT32_MIN;
+    }
+    for (uint32_t s = tid; s < cap; s += NT) {
+      hkeys[s] = EMPTY;
+      hcnts[s] = 0u;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < HPT; ++t) {
+      const int id = idv[t];
+      bool fresh = false;
+      uint32_t slot = 0;
+      if (id != INT32_MIN) {
+        if (id < 0 || id >= V) {
+          atomicOr(&s_hflags, LSS_FLAG_BAD_HISTORY);
+        } else {
+          uint32_t h = ((uint32_t)id * 2654435761u) & (cap - 1u);
+          for (uint32_t probe = 0; probe < cap; ++probe) {
+            const uint32_t old = atomicCAS(&hkeys[h], EMPTY, (uint32_t)id);
+            if (old == EMPTY || old == (uint32_t)id) {
+              atomicAdd(&hcnts[h], 1u);
+              fresh = old == EMPTY;
+              slot = h;
+              break;
+            }
+            h = (h + 1u) & (cap - 1u);
+          }
+        }
+      }
+      const uint32_t bal = __ballot_sync(0xffffffffu, fresh);
+      if (bal) {
+        const int leader = __ffs(bal) - 1;
+        uint32_t base = 0;
+        if (lane == leader) base = atomicAdd(&s_nh, (uint32_t)__popc(bal));
+        base = __shfl_sync(0xffffffffu, base, leader);
+        if (fresh) hslot[base + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)slot;
+      }
+    }
+    __syncthreads();
+    const int nh = (int)s_nh;
+    // The raw logit at every listed id (all requested at once), then the penalties.
+    int ids[HPT];
+    float raw[HPT];
+#pragma unroll
+    for (int t = 0; t < HPT; ++t) {
+      const int i = t * NT + tid;
+      ids[t] = i < nh ? (int)hkeys[hslot[i]] : -1;
+      raw[t] = ids[t] >= 0 ? load_logit(zrow, g.dtype, ids[t]) : 0.0f;
+    }
+#pragma unroll
+    for (int t = 0; t < HPT; ++t) {
+      const int i = t * NT + tid;
+      if (ids[t] >= 0) {
+        const float v = penalise(raw[t], rp, fq, pr, (int)hcnts[hslot[i]]);
+        hz[i] = v;
+        hmax = fmax_nan(hmax, v);
+        hspecial |= !(v == v) || v == INFINITY;
+      }
+    }
+  }
+  // Is id one of the row's history ids?
+  auto in_hist = [&](uint32_t id) -> bool {
+    if (!cap) return false;
+    uint32_t h = (id * 2654435761u) & (cap - 1u);
+    for (uint32_t probe = 0; probe < cap; ++probe) {
+      const uint32_t key = hkeys[h];
+      if (key == id) return true;
+      if (key == EMPTY) return false;
+      h = (h + 1u) & (cap - 1u);
+    }
+    return false;
+  };
+
   pdl_trigger();
-  pdl_wait();  // the streaming kernel's summaries, candidates and raw history values are visible
-  if (tid == 0 && g.rowflag[row]) atomicOr(a.err, g.rowflag[row]);
+  pdl_wait();  // the streaming kernel's summaries and candidates are complete and visible
+  if (tid == 0 && s_hflags) atomicOr(a.err, s_hflags);
   const uint4* sm_row = g.summ + (int64_t)row * g.MAXSL;
   if (greedy) {
     uint64_t b = 0;
@@ -261,57 +387,61 @@ __global__ void __launch_bounds__(NT, 2) lss_resolve_kernel(const RowArgs a, con
     }
     return;
   }
-  if (!bounded) {
+  if (!bounded || (hist_on && hist_long)) {
     if (tid == 0) a.defer_rows[atomicAdd(&a.counters[2], 1u)] = row;
     return;
   }
-  // One round trip for the common case: the summaries, the first SPEC slots of every slice's
-  // segment and the row's history values are requested together.
+  // One round trip for the common case: the summaries and the first SPEC slots of every
+  // slice's segment are requested together.
   const int SPEC = max(1, min(256, NT / max(nsl, 1)));
   const int ss = tid / SPEC, si = tid - ss * SPEC;
   uint64_t cspec = 0;
   if (ss < nsl) cspec = g.cand[((int64_t)row * g.MAXSL + ss) * g.SEGCAP + si];
   uint4 sm = make_uint4(0u, 0u, 0u, 0u);
   if (tid < nsl) sm = sm_row[tid];
-  const int32_t* so = g.seg2 + (int64_t)row * (g.nseg + 1);
-  const int hb = so[0], he = so[g.nseg];
-  float hz[HPT];
-  int hid[HPT];
-  float hmax = -INFINITY;
-#pragma unroll
-  for (int q = 0; q < HPT; ++q) {
-    const int e = hb + tid + q * NT;
-    hid[q] = -1;
-    hz[q] = -INFINITY;
-    if (e < he) {
-      hid[q] = a.uniq_ids[e];
-      hz[q] = penalise(g.hraw[e], rp, fq, pr, a.uniq_cnt[e]);
-      hmax = fmax_nan(hmax, hz[q]);
-    }
-  }
-  for (int e = hb + tid + HPT * NT; e < he; e += NT)
-    hmax = fmax_nan(hmax, penalise(g.hraw[e], rp, fq, pr, a.uniq_cnt[e]));
-  // Slice summaries: max key of the non-history values (all ones: NaN / +inf), flags, counts.
-  const uint32_t mkey = block_allreduce(tid < nsl ? sm.x : 0u, MaxU32(), r32);
-  const uint32_t fl = block_allreduce(tid < nsl ? sm.w : 0u, OrU32(), r32);
-  const uint32_t over = block_allreduce(tid < nsl && sm.z > (uint32_t)g.SEGCAP ? 1u : 0u, OrU32(), r32);
-  hmax = block_allreduce(hmax, MaxF(), rf);
-  // Prefix of the counts beyond the speculated slots.
-  uint32_t tot;
+  // Per slice: count, and U / T as a key (0: every finite value of the slice is a candidate).
+  uint32_t uy = 0u;
+  if (tid < nsl && sm.y > KEY_FINITE_MIN) uy = f2key(__fdiv_rn(key2f(sm.y), T));
+  const uint32_t fl = block_allreduce((tid < nsl ? sm.w : 0u) | (hspecial ? 1u : 0u) |
+                                          (tid < nsl && sm.z > (uint32_t)g.SEGCAP ? 2u : 0u),
+                                      OrU32(), r32);
   const uint32_t rest = (tid < nsl && sm.z > (uint32_t)SPEC) ? min(sm.z, (uint32_t)g.SEGCAP) - (uint32_t)SPEC : 0u;
+  uint32_t tot;
   const uint32_t pre = block_excl_scan(rest, r32, tot);
   if (tid < nsl) {
     s_pre[tid] = pre;
     s_cnt[tid] = sm.z;
+    s_uy[tid] = uy;
   }
+  if (tid == 0) s_pre[nsl] = tot;
   __syncthreads();
+  if (fl != 0u) {  // NaN / +inf (raw or penalised), or a segment overflowed
+    if (tid == 0) a.defer_rows[atomicAdd(&a.counters[2], 1u)] = row;
+    return;
+  }
+  // The candidate of flat position i beyond the speculated slots.
+  auto cand_at = [&](uint32_t i) -> uint64_t {
+    int lo_s = 0, hi_s = nsl - 1;  // last slice whose prefix is <= i
+    while (lo_s < hi_s) {
+      const int mid = (lo_s + hi_s + 1) >> 1;
+      if (s_pre[mid] <= i) lo_s = mid; else hi_s = mid - 1;
+    }
+    return g.cand[((int64_t)row * g.MAXSL + lo_s) * g.SEGCAP + SPEC + (i - s_pre[lo_s])];
+  };
+  const bool spec_ok = ss < nsl && (uint32_t)si < s_cnt[ss] && si < g.SEGCAP;
+  const bool spec_nh = spec_ok && !in_hist(~(uint32_t)cspec);
+  const uint32_t total = s_pre[nsl];
+  // Row max of z: the candidates that are not history ids, and the penalised history values.
+  float zmax = spec_nh ? key2f((uint32_t)(cspec >> 32)) : -INFINITY;
+  for (uint32_t i = tid; i < total; i += NT) {
+    const uint64_t c = cand_at(i);
+    if (!in_hist(~(uint32_t)c)) zmax = fmaxf(zmax, key2f((uint32_t)(c >> 32)));
+  }
+  zmax = block_allreduce(fmax_nan(zmax, hmax), MaxF(), rf);
   if (tid == 0) {
-    s_pre[nsl] = tot;
-    const float mz = mkey == 0xffffffffu ? NAN : key2f(mkey);
-    const float M = fmax_nan(mz, hmax);
-    const float my = __fdiv_rn(M, T);
+    const float my = __fdiv_rn(zmax, T);
     const bool special = !(my == my) || my == INFINITY || my == -INFINITY;
-    s_defer = (fl != 0u || over != 0u || special) ? 1 : 0;
+    s_defer = special ? 1 : 0;
     s_my = my;
     s_kmp = (!special && mp_on) ? minp_key(my, mp) : KEY_FINITE_MIN;
     s_n = 0u;
@@ -321,45 +451,160 @@ __global__ void __launch_bounds__(NT, 2) lss_resolve_kernel(const RowArgs a, con
     if (tid == 0) a.defer_rows[atomicAdd(&a.counters[2], 1u)] = row;
     return;
   }
-  const float my = s_my;
+  float my = s_my;
   const uint32_t Kmp = s_kmp;
+  auto push_key = [&](uint32_t yk, uint32_t low) {
+    const uint32_t pos = atomicAdd(&s_n, 1u);
+    if (pos < (uint32_t)FAST_CAP) G[pos] = ((uint64_t)yk << 32) | low;
+  };
   auto push = [&](float y, uint32_t low) {
     const uint32_t yk = f2key(y);
-    if (y > -INFINITY && yk >= Kmp) {
-      const uint32_t pos = atomicAdd(&s_n, 1u);
-      if (pos < (uint32_t)FAST_CAP) G[pos] = ((uint64_t)yk << 32) | low;
-    }
+    if (y > -INFINITY && yk >= Kmp) push_key(yk, low);
   };
-  // Streaming kernel's candidates (history positions are not among them).
-  if (ss < nsl && (uint32_t)si < s_cnt[ss] && si < g.SEGCAP)
-    push(__fdiv_rn(key2f((uint32_t)(cspec >> 32)), T), (uint32_t)cspec);
-  const uint32_t total = s_pre[nsl];
+  if (spec_nh) push(__fdiv_rn(key2f((uint32_t)(cspec >> 32)), T), (uint32_t)cspec);
   for (uint32_t i = tid; i < total; i += NT) {
-    int lo_s = 0, hi_s = nsl - 1;  // last slice whose prefix is <= i
-    while (lo_s < hi_s) {
-      const int mid = (lo_s + hi_s + 1) >> 1;
-      if (s_pre[mid] <= i) lo_s = mid; else hi_s = mid - 1;
-    }
-    const uint64_t c = g.cand[((int64_t)row * g.MAXSL + lo_s) * g.SEGCAP + SPEC + (i - s_pre[lo_s])];
-    push(__fdiv_rn(key2f((uint32_t)(c >> 32)), T), (uint32_t)c);
+    const uint64_t c = cand_at(i);
+    if (!in_hist(~(uint32_t)c)) push(__fdiv_rn(key2f((uint32_t)(c >> 32)), T), (uint32_t)c);
   }
-  // History values (penalised above).
-#pragma unroll
-  for (int q = 0; q < HPT; ++q)
-    if (hid[q] >= 0) push(__fdiv_rn(hz[q], T), ~(uint32_t)hid[q]);
-  for (int e = hb + tid + HPT * NT; e < he; e += NT)
-    push(__fdiv_rn(penalise(g.hraw[e], rp, fq, pr, a.uniq_cnt[e]), T), ~(uint32_t)a.uniq_ids[e]);
+  for (int i = tid; i < (int)s_nh; i += NT) push(__fdiv_rn(hz[i], T), ~hkeys[hslot[i]]);
   __syncthreads();
-  const uint32_t nk = s_n;
-  if (nk == 0u || nk > (uint32_t)FAST_CAP) {
+  int nk = (int)s_n;
+  if (nk == 0 || nk > FAST_CAP) {
     if (tid == 0) a.defer_rows[atomicAdd(&a.counters[2], 1u)] = row;
     return;
   }
+  // The cut: the min-p key, and for top-k rows the k-th largest kept value.
+  bool sorted = false;
+  uint32_t cut = Kmp;
+  if (tk_on && k <= nk) {
+    const int np = next_pow2(nk);
+    for (int i = nk + tid; i < np; i += NT) G[i] = 0ull;
+    __syncthreads();
+    bitonic_sort(G, np, true);
+    __syncthreads();
+    sorted = true;
+    cut = max(cut, (uint32_t)(G[k - 1] >> 32));
+  }
+  const uint32_t umax = block_allreduce(tid < nsl ? s_uy[tid] : 0u, MaxU32(), r32);
+  if (umax >= cut) {
+    // ---- re-read the slices whose threshold reaches the cut: in such a slice, the chunks whose
+    // max reaches it (the streaming kernel recorded every chunk's max), every value at or above
+    // the cut that is not a history id (the ones already among the candidates come twice and
+    // are merged below).  A row has at most C <= NT chunks, so the chunk list fits s_cnt.
+    const int ES = g.dtype == LSS_DTYPE_F32 ? 4 : 2;
+    const int VPC = g.CE * ES / 16;  // 16-byte vectors per chunk
+    // Most values lie below zc, under which z / T cannot reach the cut: they cost one compare.
+    const float zc = z_floor_for(key2f(cut), T);
+    const uint32_t zck = f2key(zc);
+    auto take = [&](float z, int idx) {
+      if (!(z >= zc) || idx >= V) return;
+      const float y = __fdiv_rn(z, T);
+      const uint32_t yk = f2key(y);
+      if (y > -INFINITY && yk >= cut && !in_hist((uint32_t)idx)) push_key(yk, ~(uint32_t)idx);
+    };
+    const bool vec_ok = (reinterpret_cast<uintptr_t>(zrow) & 15u) == 0;
+    const int64_t r0 = (int64_t)row * g.C;
+    for (int s = 0; s < nsl; ++s) {
+      if (s_uy[s] < cut) continue;
+      const int c = cf + s;
+      const int64_t ch0 = max((int64_t)c * g.N / g.G, r0);
+      const int64_t ch1 = min((int64_t)(c + 1) * g.N / g.G, r0 + g.C);
+      __syncthreads();
+      if (tid == 0) s_kmp = 0u;  // chunk-list length
+      __syncthreads();
+      for (int64_t ch = ch0 + tid; ch < ch1; ch += NT)
+        if (g.cmax[ch] >= zck) s_cnt[atomicAdd(&s_kmp, 1u)] = (uint32_t)(ch - r0);
+      __syncthreads();
+      const int nrc = (int)s_kmp;
+      if (vec_ok) {
+        // Four 16-byte vectors per thread requested at once.
+        for (int q0 = 0; q0 < nrc * VPC; q0 += 4 * NT) {
+          uint4 w[4];
+          int i0[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int q = q0 + t * NT + tid;
+            i0[t] = -1;
+            w[t] = make_uint4(0u, 0u, 0u, 0u);
+            if (q < nrc * VPC) {
+              const int cc = (int)s_cnt[q / VPC];
+              i0[t] = cc * g.CE + (q % VPC) * (16 / ES);
+              if (i0[t] + 16 / ES <= V) w[t] = reinterpret_cast<const uint4*>(zrow + (int64_t)i0[t] * ES)[0];
+            }
+          }
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            if (i0[t] < 0 || i0[t] >= V) continue;
+            if (i0[t] + 16 / ES > V) {  // the row ends inside this vector: its last values one by one
+              for (int i = i0[t]; i < V; ++i) take(load_logit(zrow, g.dtype, i), i);
+              continue;
+            }
+            const uint32_t x[4] = {w[t].x, w[t].y, w[t].z, w[t].w};
+#pragma unroll
+            for (int j2 = 0; j2 < 4; ++j2) {
+              if (ES == 4) {
+                take(__uint_as_float(x[j2]), i0[t] + j2);
+              } else if (g.dtype == LSS_DTYPE_BF16) {
+                take(__uint_as_float(x[j2] << 16), i0[t] + 2 * j2);
+                take(__uint_as_float(x[j2] & 0xffff0000u), i0[t] + 2 * j2 + 1);
+              } else {
+                take(__half2float(__ushort_as_half((uint16_t)(x[j2] & 0xffffu))), i0[t] + 2 * j2);
+                take(__half2float(__ushort_as_half((uint16_t)(x[j2] >> 16))), i0[t] + 2 * j2 + 1);
+              }
+            }
+          }
+        }
+      } else {
+        for (int q = tid; q < nrc * g.CE; q += NT) {
+          const int i = (int)s_cnt[q / g.CE] * g.CE + q % g.CE;
+          if (i < V) take(load_logit(zrow, g.dtype, i), i);
+        }
+      }
+    }
+    __syncthreads();
+    nk = (int)s_n;
+    if (nk > FAST_CAP) {
+      if (tid == 0) a.defer_rows[atomicAdd(&a.counters[2], 1u)] = row;
+      return;
+    }
+    // Sort, merge equal codes, and take the max and the min-p key again: every value at or
+    // above the old cut is now present, and the exact cut is at least the old one.
+    {
+      const int np = next_pow2(nk);
+      for (int i = nk + tid; i < np; i += NT) G[i] = 0ull;
+      __syncthreads();
+      bitonic_sort(G, np, true);
+      __syncthreads();
+      uint64_t v[PER];
+      uint32_t keep = 0;
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        const int i = tid * PER + j;
+        v[j] = i < nk ? G[i] : 0ull;
+        if (i < nk && (i == 0 || G[i - 1] != v[j])) keep |= 1u << j;
+      }
+      uint32_t all;
+      const uint32_t at = block_excl_scan((uint32_t)__popc(keep), r32, all);
+      __syncthreads();
+      uint32_t o = at;
+#pragma unroll
+      for (int j = 0; j < PER; ++j)
+        if (keep & (1u << j)) G[o++] = v[j];
+      __syncthreads();
+      nk = (int)all;
+    }
+    my = key2f((uint32_t)(G[0] >> 32));
+    const uint32_t Kmp2 = mp_on ? minp_key(my, mp) : KEY_FINITE_MIN;
+    uint32_t c2 = 0;
+    for (int i = tid; i < nk; i += NT) c2 += (uint32_t)(G[i] >> 32) >= Kmp2 ? 1u : 0u;
+    nk = (int)block_allreduce(c2, SumU32(), r32);
+    sorted = true;
+  }
   const ResolveIn in{my, tk_on, k, tp > 0.0f && tp < 1.0f, tp, u, row, V};
-  if (nk <= 32u) {
-    if (tid < 32) resolve_warp(tid < (int)nk ? G[tid] : 0ull, (int)nk, in, a, LSS_PATH_GATHER);
+  if (nk <= 32) {
+    if (tid < 32) resolve_warp(tid < nk ? G[tid] : 0ull, nk, in, a, LSS_PATH_GATHER);
   } else {
-    resolve_block<FAST_CAP>(G, E, (int)nk, in, a, rs, LSS_PATH_GATHER);
+    resolve_block<FAST_CAP>(G, E, nk, in, a, rs, LSS_PATH_GATHER, sorted);
   }
 }
 

@@ -126,7 +126,6 @@ constexpr int MAX_VOCAB = MAXCL * (TILE_MAX_BYTES / 4);
 static int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
 struct Plan {
-  int nseg;                   // history segments per row (SEGV logits each)
   int MAXSL;                  // slices per row the workspace reserves (either logit width)
   int CL, TE;                 // second kernel: CTAs per row, logits per CTA
   int slow_tile, slow_smem;
@@ -155,7 +154,6 @@ static int slow_extra(int CL) {
 
 static Plan make_plan(int B, int V) {
   Plan pl{};
-  pl.nseg = (V + SEGV - 1) / SEGV;
   pl.MAXSL = std::max(max_slices(B, chunks_per_row(V, 4)), max_slices(B, chunks_per_row(V, 2)));
   int CL = 1;
   while (CL < MAXCL && round_up((V + CL - 1) / CL, 16) * 4 > TILE_TARGET_BYTES) CL <<= 1;
@@ -167,14 +165,11 @@ static Plan make_plan(int B, int V) {
 }
 
 // Workspace: header (word 0 error flags, word 2 deferred-row count), row path codes, the
-// streaming kernel's slice summaries and candidate segments, the per-slice segments of the
-// unique history pairs for the second kernel and the per-segment offsets for the streaming
-// kernel, per-row history flags, the deferred-row list, the pair arrays (ids, counts, raw
-// logits) and the global hash table for rows with long histories.  row_path sits at a fixed
-// offset.
+// streaming kernel's slice summaries, candidate segments and chunk maxima, the second kernel's per-slice
+// segments of the unique history pairs, the deferred-row list, the pair arrays (ids, counts)
+// and the global hash table for rows with long histories.  row_path sits at a fixed offset.
 struct WsLayout {
-  size_t header, row_path, summ, cand, seg_off, seg2, pblk, rowflag, defer_rows, uniq_ids, uniq_cnt, hraw, gkeys,
-      gcnts, total;
+  size_t header, row_path, summ, cand, cmax, seg_off, defer_rows, uniq_ids, uniq_cnt, gkeys, gcnts, total;
 };
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 static WsLayout ws_layout(int B, int V, int64_t H) {
@@ -187,14 +182,11 @@ static WsLayout ws_layout(int B, int V, int64_t H) {
   L.row_path = o; o = align256(o + 4 * b);
   L.summ = o; o = align256(o + 16 * slices);
   L.cand = o; o = align256(o + 8 * slices * (size_t)ST_SEGCAP);
+  L.cmax = o; o = align256(o + 4 * b * (size_t)chunks_per_row(std::max(V, 1), 2));
   L.seg_off = o; o = align256(o + 4 * b * (MAXCL + 1));
-  L.seg2 = o; o = align256(o + 4 * b * (size_t)(pl.nseg + 1));
-  L.pblk = o; o = align256(o + 32 * b * (size_t)pl.nseg);
-  L.rowflag = o; o = align256(o + 4 * b);
   L.defer_rows = o; o = align256(o + 4 * b);
   L.uniq_ids = o; o = align256(o + 4 * (h + 4));
   L.uniq_cnt = o; o = align256(o + 4 * (h + 4));
-  L.hraw = o; o = align256(o + 4 * (h + 4));
   L.gkeys = o; o = align256(o + 8 * h);
   L.gcnts = o; o = align256(o + 8 * h);
   L.total = o;
@@ -317,9 +309,22 @@ static cudaError_t launch_rows(StreamArgs sa, const RowArgs& ra, GatherArgs ga, 
   const int G = (int)std::min<int64_t>(nctas, sa.N);
   // Both kernels derive a row's slices from the same split of the N chunks over G CTAs.
   ga.G = G;
-  e = launch_pdl(lss_stream_kernel<DT>, (unsigned)G, (unsigned)ST_NT, (size_t)smem, 1, st, sa);
+  // The first kernel of a call: an ordinary launch, so that it starts after everything before
+  // it on the stream (the producer of the logits included) has finished.
+  lss_stream_kernel<DT><<<(unsigned)G, (unsigned)ST_NT, (size_t)smem, st>>>(sa);
+  e = cudaGetLastError();
   if (e != cudaSuccess || scan_only) return e;
-  e = launch_pdl(lss_resolve_kernel, (unsigned)B, (unsigned)NT, (size_t)0, 1, st, ra, ga);
+  {
+    static int resolve_smem_set[64] = {};
+    const int dev = current_device();
+    std::lock_guard<std::mutex> lock(g_cfg_mu);
+    if (!resolve_smem_set[dev]) {
+      e = cudaFuncSetAttribute(lss_resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, resolve_smem_bytes());
+      if (e != cudaSuccess) return e;
+      resolve_smem_set[dev] = 1;
+    }
+  }
+  e = launch_pdl(lss_resolve_kernel, (unsigned)B, (unsigned)NT, (size_t)resolve_smem_bytes(), 1, st, ra, ga);
   if (e != cudaSuccess) return e;
   int ncs = 0;
   switch (pl.CL) {
@@ -428,54 +433,14 @@ int lss_sample_prepare(int B, int V, const float* temperature, const int32_t* to
                        const float* repetition_penalty, const float* frequency_penalty,
                        const float* presence_penalty, const int32_t* hist_offsets, const int32_t* hist_ids,
                        int64_t hist_total, void* workspace, size_t workspace_bytes, void* stream) {
+  // The history pairs are built by the resolve kernel of lss_sample_rows, which reads them
+  // while the streaming kernel runs; this stage checks the arguments and launches nothing.
+  (void)stream;
   int rc = check_common(B, V, hist_total, hist_offsets, workspace, workspace_bytes);
   if (rc != LSS_OK || B == 0) return rc;
   if (!temperature || !top_k || !min_p || !repetition_penalty || !frequency_penalty || !presence_penalty)
     return LSS_ERR_INVALID_ARG;
   if (hist_total > 0 && !hist_ids) return LSS_ERR_INVALID_ARG;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  unsigned char* ws = reinterpret_cast<unsigned char*>(workspace);
-  const WsLayout L = ws_layout(B, V, hist_total);
-  const Plan pl = make_plan(B, V);
-  HistArgs h{};
-  h.r.B = B;
-  h.r.V = V;
-  h.r.use_hist = hist_total > 0 ? 1 : 0;
-  h.r.H = (int)hist_total;
-  h.r.temperature = temperature;
-  h.r.top_k = top_k;
-  h.r.min_p = min_p;
-  h.r.rep = repetition_penalty;
-  h.r.freq = frequency_penalty;
-  h.r.pres = presence_penalty;
-  h.r.hist_off = hist_offsets;
-  h.r.hist_ids = hist_ids;
-  h.r.uniq_ids = reinterpret_cast<int32_t*>(ws + L.uniq_ids);
-  h.r.uniq_cnt = reinterpret_cast<int32_t*>(ws + L.uniq_cnt);
-  h.r.gkeys = reinterpret_cast<uint32_t*>(ws + L.gkeys);
-  h.r.gcnts = reinterpret_cast<uint32_t*>(ws + L.gcnts);
-  h.S = pl.nseg;
-  h.TS = SEGV;
-  h.seg2 = reinterpret_cast<int32_t*>(ws + L.seg2);
-  h.pblk = reinterpret_cast<int32_t*>(ws + L.pblk);
-  h.rowflag = reinterpret_cast<uint32_t*>(ws + L.rowflag);
-  h.header = reinterpret_cast<uint32_t*>(ws + L.header);
-  // K0 also clears the header (error flags, deferred-row count) for this call.
-  {
-    static KernelCfg hist_cfg{};
-    const int smem = hist_smem_bytes(V);
-    const int dev = current_device();
-    std::lock_guard<std::mutex> lock(g_cfg_mu);
-    if (hist_cfg.smem[dev] < smem) {
-      if (cudaFuncSetAttribute(lss_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
-        cudaGetLastError();
-        return LSS_ERR_CUDA;
-      }
-      hist_cfg.smem[dev] = smem;
-    }
-  }
-  lss_hist_kernel<<<B, HIST_NT, hist_smem_bytes(V), st>>>(h);
-  if (cudaGetLastError() != cudaSuccess) return LSS_ERR_CUDA;
   return LSS_OK;
 }
 
@@ -510,18 +475,13 @@ static int sample_rows(const void* logits, int dtype, int B, int V, int64_t row_
   sa.C = chunks_per_row(V, es);
   sa.N = (int64_t)B * sa.C;
   sa.MAXSL = pl.MAXSL;
-  sa.nseg = pl.nseg;
-  sa.use_hist = hist_total > 0 ? 1 : 0;
   sa.temperature = temperature;
   sa.top_k = top_k;
   sa.min_p = min_p;
-  sa.seg2 = reinterpret_cast<const int32_t*>(ws + L.seg2);
-  sa.pblk = reinterpret_cast<const int32_t*>(ws + L.pblk);
-  sa.uniq_ids = reinterpret_cast<const int32_t*>(ws + L.uniq_ids);
-  sa.hraw = reinterpret_cast<float*>(ws + L.hraw);
   sa.summ = reinterpret_cast<uint4*>(ws + L.summ);
   sa.cand = reinterpret_cast<uint64_t*>(ws + L.cand);
-  sa.err = header;
+  sa.cmax = reinterpret_cast<uint32_t*>(ws + L.cmax);
+  sa.header = header;
   RowArgs a{};
   a.logits = logits;
   a.row_stride = row_stride;
@@ -562,10 +522,9 @@ static int sample_rows(const void* logits, int dtype, int B, int V, int64_t row_
   ga.C = sa.C;
   ga.N = sa.N;
   ga.G = 1;  // set at launch to the streaming kernel's grid
-  ga.nseg = pl.nseg;
-  ga.seg2 = sa.seg2;
-  ga.hraw = sa.hraw;
-  ga.rowflag = reinterpret_cast<const uint32_t*>(ws + L.rowflag);
+  ga.CE = ST_CB / es;
+  ga.cmax = sa.cmax;
+  ga.dtype = dtype;
   cudaError_t e;
   switch (dtype) {
     case LSS_DTYPE_F32: e = launch_rows<LSS_DTYPE_F32>(sa, a, ga, pl, B, st, scan_only); break;

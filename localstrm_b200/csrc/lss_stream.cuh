@@ -9,27 +9,30 @@
 // Inside a CTA every warp works alone: warp w takes chunks w, w + 16, w + 32, ... of the range,
 // each through its own ring of ST_R shared-memory stages filled by bulk async copies that its
 // lane 0 issues (and bounded mbarrier waits), so that a warp never waits for another warp and
-// the CTA keeps 16 x (ST_R - 1) chunks in flight.  Per chunk the warp
-//   * excludes the row's history positions (K0's unique ids of the chunk's segments): their raw
-//     values go to hraw[] for the resolve kernel, which applies the penalties there
-//     (sampling.py:55-66), and the stage holds -inf in their place;
-//   * takes the chunk max of the remaining values and folds it into the slice's running max
-//     (a shared atomic max in the slice's slot);
+// the CTA keeps 16 x (ST_R - 1) chunks in flight.  The pass reads nothing but the logits and
+// the row parameters, so it is the first kernel of a call and starts streaming at once; the
+// history (sampling.py:52-66) is left to the resolve kernel.  Per chunk the warp
+//   * takes the chunk max of the raw values and folds it into the slice's running max (a
+//     shared atomic max in the slice's slot);
 //   * for top-k rows, counts its values above the current threshold into the slice's shared
 //     count histogram (bins of 1/16 nat of y below a fixed reference) and raises the slice's
 //     top-k threshold from it;
-//   * writes the values at or above the candidate threshold into the slice's segment.
-// The last warp to finish a slice writes the slice summary (running max or argmax code,
-// candidate count, flags) and hands the slot to a later slice.
+//   * writes the values at or above the candidate threshold into the slice's segment, raises
+//     the slice's record of the largest threshold used (a shared atomic max), and records the
+//     chunk's max (so that a slice the resolve kernel must re-read costs it only the chunks
+//     that can hold a survivor).
+// The last warp to finish a slice writes the slice summary (running max or argmax code, the
+// largest candidate threshold, candidate count, flags) and hands the slot to a later slice.
 //
-// Why the candidates are a superset of the row's survivors: every threshold is a lower bound
-// of the exact one.  The running max is a max over a subset of the row's non-history values,
-// so the min-p floor taken from it lies below the exact floor (the exact row max, which also
-// covers the history values, is only larger).  The top-k threshold lies below a value that at
-// least k values of the slice reach, so every value among the k largest of the row that lies
-// in the slice is kept.  History values are handled by the resolve kernel in full.  Thresholds
-// are taken on z (y = z / T is monotone) with margins that cover every rounding of the exact
-// filter, which the resolve kernel applies.
+// What the resolve kernel can rely on: every value of the slice that is not a candidate lies
+// below the slice's largest threshold U (or is -inf).  Without penalties every threshold is a
+// lower bound of the exact one (the min-p floor is taken from a running max over a subset of
+// the row, the top-k threshold lies below a value that k values of the slice reach), so the
+// candidates hold every survivor.  With penalties a history value counts here with its raw
+// value, which can raise a threshold above the exact one; the resolve kernel, which knows the
+// penalised values, checks its exact cut against U and re-reads a slice whose U lies at or
+// above it.  Thresholds are taken on z (y = z / T is monotone) with margins that cover every
+// rounding of the exact filter, which the resolve kernel applies.
 #pragma once
 
 #include <type_traits>
@@ -46,14 +49,11 @@ constexpr int ST_NSLOT = 8;                   // slice slots per CTA
 constexpr int ST_SEGCAP = 1024;               // candidate slots per slice
 constexpr int ST_ROWTAB = 64;                 // rows whose parameters a CTA keeps in shared memory
 constexpr int ST_GCAP = 160;                  // largest grid the workspace layout allows for
-constexpr int SEGV = 1024;                    // history segment: K0 groups the pairs per SEGV logits
-constexpr int ST_PBW = 8;                     // words of a segment's pair block (K0)
-constexpr int ST_NBK = ST_CB / 2 / SEGV;      // pair blocks a chunk may need (2 for 16-bit logits)
-constexpr int ST_SB = ST_CB + ST_NBK * ST_PBW * 4;  // bytes of a stage: the chunk, then its pair blocks
+constexpr int ST_SB = ST_CB;                  // bytes of a stage: one chunk
 constexpr int ST_STAGE_BYTES = ST_NW * ST_R * ST_SB;
 
 constexpr int ITEM_SKIP = 1, ITEM_GREEDY = 2, ITEM_SAMPLE = 3;
-// Summary flags: NaN / +inf among the slice's non-history values.
+// Summary flags: NaN / +inf among the slice's values.
 constexpr uint32_t SUM_SPECIAL = 1u;
 
 struct __align__(16) SliceSlot {
@@ -66,7 +66,8 @@ struct __align__(16) SliceSlot {
   uint32_t taukey;      // top-k: key of the current threshold (0: none)
   uint32_t above;       // top-k: counted values above the reference
   unsigned long long best;  // greedy: argmax code
-  uint32_t pad[2];
+  uint32_t ukey;        // key of the largest candidate threshold any chunk used (0: none yet)
+  uint32_t pad;
   uint32_t hist[NBIN];  // top-k: counted values by depth below the reference, 1/16 nat of y per bin
 };
 
@@ -87,18 +88,13 @@ struct StreamArgs {
   int B, V, C;          // C: chunks per row
   int64_t N;            // B * C
   int MAXSL;            // slices per row reserved in the workspace (summary and segment stride)
-  int nseg;             // history segments per row (K0)
-  int use_hist;
   const float* temperature;
   const int32_t* top_k;
   const float* min_p;
-  const int32_t* seg2;  // [B][nseg + 1]: absolute offsets of each segment's pairs (K0)
-  const int32_t* pblk;  // [B][nseg][ST_PBW]: per segment {first pair, pairs, first six ids} (K0)
-  const int32_t* uniq_ids;
-  float* hraw;          // raw logit at each pair's id (same index as uniq_ids)
-  uint4* summ;          // [B][MAXSL]: {max key | argmax code lo, argmax code hi, count, flags}
+  uint4* summ;          // [B][MAXSL]: {max key | argmax code lo, threshold key | argmax code hi, count, flags}
   uint64_t* cand;       // [B][MAXSL][ST_SEGCAP]: (key(z) << 32) | ~index
-  uint32_t* err;
+  uint32_t* cmax;       // [B * C]: key of each sampled chunk's max (all ones: NaN / +inf)
+  uint32_t* header;     // workspace status words (word 0: error flags; word 2: deferred rows), cleared here
 };
 
 __host__ __device__ constexpr int stream_smem_bytes() {
@@ -168,6 +164,10 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
       if (row0 + i < a.B) rtab[i] = make_row_prm(a, row0 + i, g0, g1);
     if (tid < ST_NW * ST_R) fence_barrier_init();
     if (tid == 0) *abort_w = 0u;
+    // This call's status: the error flags and the deferred-row count start at zero.  (The
+    // resolve kernel counts deferred rows only after it has waited for this grid; the flags
+    // other CTAs may raise come from waits of seconds.)
+    if (blockIdx.x == 0 && tid < 64) a.header[tid] = 0u;
   }
   __syncthreads();
   pdl_trigger();  // the resolve kernel may launch; it waits for this grid before reading
@@ -203,21 +203,13 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
     const char* src = reinterpret_cast<const char*>(a.logits) + ((int64_t)row * a.row_stride + lo) * ES;
     const int mode = prm_of(row).mode;
     const int nb = (mode != ITEM_SKIP && (reinterpret_cast<uintptr_t>(src) & 15) == 0) ? ((n * ES) & ~15) : 0;
-    // The pair blocks of the chunk's segments travel with it (sampled rows with histories).
-    const int seg0 = lo / SEGV;
-    const int nbk = (mode == ITEM_SAMPLE && a.use_hist) ? min(ST_NBK, a.nseg - seg0) : 0;
-    mbar_expect_tx(&wbar[s], (uint32_t)(nb + nbk * ST_PBW * 4));
-    unsigned char* dst = wst + s * ST_SB;
-    if (nb > 0) bulk_g2s(dst, src, (uint32_t)nb, &wbar[s]);
-    if (nbk > 0)
-      bulk_g2s(dst + ST_CB, a.pblk + ((int64_t)row * a.nseg + seg0) * ST_PBW, (uint32_t)(nbk * ST_PBW * 4), &wbar[s]);
+    mbar_expect_tx(&wbar[s], (uint32_t)nb);
+    if (nb > 0) bulk_g2s(wst + s * ST_SB, src, (uint32_t)nb, &wbar[s]);
   };
-  // The first chunks stream in while K0 still runs: they read nothing K0 writes.
   if (lane == 0)
     for (int i = 0; i < ST_R; ++i)
       if (gw + (int64_t)i * ST_NW < g1) issue(adv(pw, i * ST_NW), i);
   __syncwarp();
-  pdl_wait();  // K0's pairs and segment offsets are complete and visible
 
   auto elem = [&](const unsigned char* st, int i) -> float {
     if (DT == LSS_DTYPE_F32) return reinterpret_cast<const float*>(st)[i];
@@ -280,7 +272,7 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
     const int ls = row - row0;
     if (!warp_mbar_wait(&wbar[s], par)) {
       if (lane == 0) {
-        atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
+        atomicOr(a.header, LSS_FLAG_TMA_TIMEOUT);
         *abort_w = 1u;
       }
       __syncwarp();
@@ -306,7 +298,7 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
       __threadfence_block();
       if (st2 == 2u) {
         if (lane == 0) {
-          atomicOr(a.err, LSS_FLAG_INTERNAL);
+          atomicOr(a.header, LSS_FLAG_INTERNAL);
           *abort_w = 1u;
         }
         __syncwarp();
@@ -332,47 +324,6 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
         for (int e = n + lane; e < CE; e += 32) {
           set_neg_inf(st, e);
           wrote = true;
-        }
-        __syncwarp();
-      }
-      // History positions of the chunk: the raw value goes to hraw (the resolve kernel applies
-      // the penalties) and the stage holds -inf in its place.  The chunk's pair blocks (one per
-      // segment) arrived with it: the first pair's index, the number of pairs, the first six
-      // ids; further ids of a segment come from the pair array.
-      if (P.mode == ITEM_SAMPLE && a.use_hist) {
-        const int32_t* blk = reinterpret_cast<const int32_t*>(st + ST_CB);
-        const int nbk = min(ST_NBK, a.nseg - lo / SEGV);
-        for (int sb = 0; sb < nbk; ++sb) {
-          const int base = blk[sb * ST_PBW], cnt = blk[sb * ST_PBW + 1];
-          if (cnt <= 0) continue;
-          if (lane < min(cnt, ST_PBW - 2)) {
-            const int pos = blk[sb * ST_PBW + 2 + lane] - lo;
-            if ((unsigned)pos < (unsigned)n) {
-              a.hraw[base + lane] = elem(st, pos);
-              set_neg_inf(st, pos);
-              wrote = true;
-            }
-          }
-          // Further ids: eight per lane requested at once, so that a segment with hundreds of
-          // pairs (a row's first chunk) costs one or two round trips.
-          for (int e0 = ST_PBW - 2; e0 < cnt; e0 += 32 * 8) {
-            int idv[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int e = e0 + 32 * k + lane;
-              idv[k] = e < cnt ? a.uniq_ids[base + e] : -1;
-            }
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int e = e0 + 32 * k + lane;
-              const int pos = idv[k] - lo;
-              if (e < cnt && (unsigned)pos < (unsigned)n) {
-                a.hraw[base + e] = elem(st, pos);
-                set_neg_inf(st, pos);
-                wrote = true;
-              }
-            }
-          }
         }
         __syncwarp();
       }
@@ -414,6 +365,7 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
         for (int j = 1; j < NV; ++j) lm = fmax_nan(lm, vmx[j]);
         const float cmax = wred(lm, MaxF());
         const uint32_t ck = (!(cmax == cmax) || cmax == INFINITY) ? 0xffffffffu : f2key(cmax);
+        if (lane == 0) a.cmax[g] = ck;
         uint32_t mk = 0;
         if (lane == 0) {
           // The running max as far as this warp can see it: its own chunk's and what the slot
@@ -539,6 +491,7 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
           // values at or above the threshold in a bit mask, and writes only those, reading the
           // value back from the stage.
           thr = fmaxf(thr, -FLT_MAX);
+          if (lane == 0) atomicMax(&sl->ukey, f2key(thr));
           const bool mine = lm >= thr;
           if (__ballot_sync(0xffffffffu, mine)) {
             MaskT m = 0;
@@ -603,7 +556,7 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
           const unsigned long long b = vs->best;
           sm = make_uint4((uint32_t)b, (uint32_t)(b >> 32), 0u, 0u);
         } else {
-          sm = make_uint4(vs->maxkey, 0u, vs->count, vs->flags);
+          sm = make_uint4(vs->maxkey, vs->ukey, vs->count, vs->flags);
         }
         a.summ[(int64_t)row * a.MAXSL + jsl] = sm;
       }

@@ -213,6 +213,38 @@ def headline(seed: int = 0, B: int = 256, V: int = QWEN_VOCAB) -> Workload:
     return w
 
 
+def history_on_top(seed: int = 0, B: int = 32, V: int = QWEN_VOCAB, dtype: str = "f32") -> Workload:
+    """Rows whose largest raw logits are history tokens, as in repetitive decoding.
+
+    N(0, 2^2) background; per row 24 head tokens raised by +6 .. +11 (distinct random ids), of
+    which the 12 largest are in the row's history (1 to 6 times each) together with 400 ids ~
+    Zipf(1.1).  Repetition 1.6, frequency 0.6, presence 0.4 push those tokens below the others.
+    Parameters cycle over four kinds of row: min-p 0.05; top-k 20; top-k 50 with min-p 0.02;
+    top-k 100 with top-p 0.9.  Temperature 0.8.
+    """
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((B, V), dtype=np.float32) * np.float32(2.0)).astype(np.float32)
+    hists = []
+    for r in range(B):
+        head = rng.choice(V, size=min(24, V), replace=False)
+        boost = np.sort(rng.uniform(6.0, 11.0, size=len(head)).astype(np.float32))[::-1]
+        x[r, head] += boost
+        top = head[:12]
+        reps = [np.full(int(rng.integers(1, 7)), t, np.int32) for t in top]
+        h = np.concatenate(reps + [_zipf_ids(rng, 1.1, 400, V)])
+        rng.shuffle(h)
+        hists.append(h.astype(np.int32))
+    x = round_to_dtype(x, dtype)
+    offs, ids = _csr(hists)
+    kind = np.arange(B) % 4
+    top_k = np.select([kind == 1, kind == 2, kind == 3], [20, 50, 100], 0).astype(np.int32)
+    min_p = np.select([kind == 0, kind == 2], [0.05, 0.02], 0.0).astype(np.float32)
+    top_p = np.where(kind == 3, 0.9, 1.0).astype(np.float32)
+    return Workload("hist_on_top", x, dtype, np.full(B, 0.8, np.float32), top_k, top_p, min_p,
+                    np.full(B, 1.6, np.float32), np.full(B, 0.6, np.float32),
+                    np.full(B, 0.4, np.float32), offs, ids, _uniforms(seed, B), seed)
+
+
 def by_name(name: str, **kw) -> Workload:
     return {"cfg1": config1, "cfg2": config2, "cfg3": config3, "cfg4": config4,
             "cfg5": config5, "headline": headline}[name](**kw)

@@ -97,6 +97,22 @@ def test_config2_bf16():
 
 
 @needs_cuda
+@pytest.mark.parametrize("dtype,V,pad", [("f32", wl.QWEN_VOCAB, 0), ("bf16", wl.QWEN_VOCAB, 0),
+                                         ("f32", 40_001, 0), ("f32", 40_001, 3), ("bf16", 40_001, 1)])
+def test_history_on_top_tokens(dtype, V, pad):
+    """The rows' largest raw logits are history tokens that the penalties push down: the
+    streaming pass counts them with their raw values, so its thresholds lie above the exact
+    cut, and the resolve kernel must re-read chunks of those slices (16-byte loads, or one by
+    one for rows that start off a 16-byte boundary; ragged row ends).  Parity on every row,
+    and the rows stay in the resolve kernel (path 3) instead of going to the second kernel."""
+    w = wl.history_on_top(seed=11, V=V, dtype=dtype)
+    out = G.run(w, dtype=dtype, row_stride=(V + pad) if pad else None)
+    assert out["flags"] == 0
+    stats = check_workload(w, out)
+    assert stats.get(3, 0) == w.B, stats
+
+
+@needs_cuda
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 def test_half_dtypes_match_upcast(dtype):
     w = wl.config1(seed=5)
