@@ -257,6 +257,7 @@ __global__ void __launch_bounds__(NT, 2) lss_resolve_kernel(const RowArgs a, con
   __shared__ uint32_t s_pre[NT + 1];
   __shared__ uint32_t s_cnt[NT];
   __shared__ uint32_t s_uy[NT];
+  __shared__ uint32_t s_rbm[NT / 32];
   __shared__ uint32_t s_n, s_kmp, s_nh, s_hflags;
   __shared__ int s_defer;
   __shared__ float s_my;
@@ -473,92 +474,157 @@ __global__ void __launch_bounds__(NT, 2) lss_resolve_kernel(const RowArgs a, con
     if (tid == 0) a.defer_rows[atomicAdd(&a.counters[2], 1u)] = row;
     return;
   }
+  // Block helpers over G[0, n): the k-th largest key (radix select, eight bits per pass, the
+  // bins in s_pre), and an in-place compaction of the entries a predicate keeps.
+  auto kth_largest = [&](int n, int kk) -> uint32_t {
+    uint32_t prefix = 0u, mask = 0u;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = tid; b < 256; b += NT) s_pre[b] = 0u;
+      __syncthreads();
+      for (int i = tid; i < n; i += NT) {
+        const uint32_t key = (uint32_t)(G[i] >> 32);
+        if ((key & mask) == prefix) atomicAdd(&s_pre[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (tid < 32) {
+        // Lane l holds bins 255 - 8l .. 248 - 8l (largest digits first).
+        uint32_t c8[8], loc = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          c8[q] = s_pre[255 - (8 * lane + q)];
+          loc += c8[q];
+        }
+        uint32_t incl = loc;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const unsigned hit = __ballot_sync(0xffffffffu, incl >= (uint32_t)kk);
+        const int L = hit ? __ffs(hit) - 1 : 31;
+        if (lane == L) {
+          uint32_t acc = incl - loc;
+          int d = 0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            if (acc + c8[q] >= (uint32_t)kk) {
+              d = 255 - (8 * lane + q);
+              break;
+            }
+            acc += c8[q];
+          }
+          s_pre[256] = (uint32_t)d;
+          s_pre[257] = acc;  // entries with a larger digit
+        }
+      }
+      __syncthreads();
+      prefix |= s_pre[256] << shift;
+      mask |= 255u << shift;
+      kk -= (int)s_pre[257];
+      __syncthreads();
+    }
+    return prefix;
+  };
+  auto compact = [&](int n, auto keep_fn) -> int {
+    uint64_t v[PER];
+    uint32_t keep = 0;
+#pragma unroll
+    for (int j2 = 0; j2 < PER; ++j2) {
+      const int i = tid * PER + j2;
+      v[j2] = i < n ? G[i] : 0ull;
+      if (i < n && keep_fn(v[j2])) keep |= 1u << j2;
+    }
+    uint32_t all;
+    const uint32_t at = block_excl_scan((uint32_t)__popc(keep), r32, all);
+    __syncthreads();
+    uint32_t o = at;
+#pragma unroll
+    for (int j2 = 0; j2 < PER; ++j2)
+      if (keep & (1u << j2)) G[o++] = v[j2];
+    __syncthreads();
+    return (int)all;
+  };
   // The cut: the min-p key, and for top-k rows the k-th largest kept value.
-  bool sorted = false;
   uint32_t cut = Kmp;
-  if (tk_on && k <= nk) {
-    const int np = next_pow2(nk);
-    for (int i = nk + tid; i < np; i += NT) G[i] = 0ull;
-    __syncthreads();
-    bitonic_sort(G, np, true);
-    __syncthreads();
-    sorted = true;
-    cut = max(cut, (uint32_t)(G[k - 1] >> 32));
-  }
+  if (tk_on && k <= nk) cut = max(cut, kth_largest(nk, k));
   const uint32_t umax = block_allreduce(tid < nsl ? s_uy[tid] : 0u, MaxU32(), r32);
   if (umax >= cut) {
     // ---- re-read the slices whose threshold reaches the cut: in such a slice, the chunks whose
-    // max reaches it (the streaming kernel recorded every chunk's max), every value at or above
-    // the cut that is not a history id (the ones already among the candidates come twice and
-    // are merged below).  A row has at most C <= NT chunks, so the chunk list fits s_cnt.
+    // max reaches it (the streaming kernel recorded every chunk's max).  Their candidates leave
+    // G, and every value of theirs at or above the cut that is not a history id comes back.  A
+    // row has at most C <= NT chunks: the chunk list fits s_cnt and its bitmap s_rbm.
     const int ES = g.dtype == LSS_DTYPE_F32 ? 4 : 2;
     const int VPC = g.CE * ES / 16;  // 16-byte vectors per chunk
     // Most values lie below zc, under which z / T cannot reach the cut: they cost one compare.
     const float zc = z_floor_for(key2f(cut), T);
     const uint32_t zck = f2key(zc);
+    const int64_t r0 = (int64_t)row * g.C;
+    for (int w2 = tid; w2 < NT / 32; w2 += NT) s_rbm[w2] = 0u;
+    if (tid == 0) s_kmp = 0u;  // chunk-list length
+    __syncthreads();
+    for (int ch = tid; ch < g.C; ch += NT) {
+      const int sl = resolve_cta_of_chunk(r0 + ch, g.N, g.G) - cf;
+      if (s_uy[sl] >= cut && g.cmax[r0 + ch] >= zck) {
+        s_cnt[atomicAdd(&s_kmp, 1u)] = (uint32_t)ch;
+        atomicOr(&s_rbm[ch >> 5], 1u << (ch & 31));
+      }
+    }
+    __syncthreads();
+    const int nrc = (int)s_kmp;
+    nk = compact(nk, [&](uint64_t c) {
+      const uint32_t idx = ~(uint32_t)c;
+      const int ch = (int)(idx / (uint32_t)g.CE);
+      return !((s_rbm[ch >> 5] >> (ch & 31)) & 1u) || in_hist(idx);
+    });
+    if (tid == 0) s_n = (uint32_t)nk;
+    __syncthreads();
     auto take = [&](float z, int idx) {
       if (!(z >= zc) || idx >= V) return;
       const float y = __fdiv_rn(z, T);
       const uint32_t yk = f2key(y);
       if (y > -INFINITY && yk >= cut && !in_hist((uint32_t)idx)) push_key(yk, ~(uint32_t)idx);
     };
-    const bool vec_ok = (reinterpret_cast<uintptr_t>(zrow) & 15u) == 0;
-    const int64_t r0 = (int64_t)row * g.C;
-    for (int s = 0; s < nsl; ++s) {
-      if (s_uy[s] < cut) continue;
-      const int c = cf + s;
-      const int64_t ch0 = max((int64_t)c * g.N / g.G, r0);
-      const int64_t ch1 = min((int64_t)(c + 1) * g.N / g.G, r0 + g.C);
-      __syncthreads();
-      if (tid == 0) s_kmp = 0u;  // chunk-list length
-      __syncthreads();
-      for (int64_t ch = ch0 + tid; ch < ch1; ch += NT)
-        if (g.cmax[ch] >= zck) s_cnt[atomicAdd(&s_kmp, 1u)] = (uint32_t)(ch - r0);
-      __syncthreads();
-      const int nrc = (int)s_kmp;
-      if (vec_ok) {
-        // Four 16-byte vectors per thread requested at once.
-        for (int q0 = 0; q0 < nrc * VPC; q0 += 4 * NT) {
-          uint4 w[4];
-          int i0[4];
+    if ((reinterpret_cast<uintptr_t>(zrow) & 15u) == 0) {
+      // Four 16-byte vectors per thread requested at once.
+      for (int q0 = 0; q0 < nrc * VPC; q0 += 4 * NT) {
+        uint4 w[4];
+        int i0[4];
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int q = q0 + t * NT + tid;
-            i0[t] = -1;
-            w[t] = make_uint4(0u, 0u, 0u, 0u);
-            if (q < nrc * VPC) {
-              const int cc = (int)s_cnt[q / VPC];
-              i0[t] = cc * g.CE + (q % VPC) * (16 / ES);
-              if (i0[t] + 16 / ES <= V) w[t] = reinterpret_cast<const uint4*>(zrow + (int64_t)i0[t] * ES)[0];
-            }
+        for (int t = 0; t < 4; ++t) {
+          const int q = q0 + t * NT + tid;
+          i0[t] = -1;
+          w[t] = make_uint4(0u, 0u, 0u, 0u);
+          if (q < nrc * VPC) {
+            i0[t] = (int)s_cnt[q / VPC] * g.CE + (q % VPC) * (16 / ES);
+            if (i0[t] + 16 / ES <= V) w[t] = reinterpret_cast<const uint4*>(zrow + (int64_t)i0[t] * ES)[0];
           }
+        }
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            if (i0[t] < 0 || i0[t] >= V) continue;
-            if (i0[t] + 16 / ES > V) {  // the row ends inside this vector: its last values one by one
-              for (int i = i0[t]; i < V; ++i) take(load_logit(zrow, g.dtype, i), i);
-              continue;
-            }
-            const uint32_t x[4] = {w[t].x, w[t].y, w[t].z, w[t].w};
+        for (int t = 0; t < 4; ++t) {
+          if (i0[t] < 0 || i0[t] >= V) continue;
+          if (i0[t] + 16 / ES > V) {  // the row ends inside this vector: its last values one by one
+            for (int i = i0[t]; i < V; ++i) take(load_logit(zrow, g.dtype, i), i);
+            continue;
+          }
+          const uint32_t x[4] = {w[t].x, w[t].y, w[t].z, w[t].w};
 #pragma unroll
-            for (int j2 = 0; j2 < 4; ++j2) {
-              if (ES == 4) {
-                take(__uint_as_float(x[j2]), i0[t] + j2);
-              } else if (g.dtype == LSS_DTYPE_BF16) {
-                take(__uint_as_float(x[j2] << 16), i0[t] + 2 * j2);
-                take(__uint_as_float(x[j2] & 0xffff0000u), i0[t] + 2 * j2 + 1);
-              } else {
-                take(__half2float(__ushort_as_half((uint16_t)(x[j2] & 0xffffu))), i0[t] + 2 * j2);
-                take(__half2float(__ushort_as_half((uint16_t)(x[j2] >> 16))), i0[t] + 2 * j2 + 1);
-              }
+          for (int j2 = 0; j2 < 4; ++j2) {
+            if (ES == 4) {
+              take(__uint_as_float(x[j2]), i0[t] + j2);
+            } else if (g.dtype == LSS_DTYPE_BF16) {
+              take(__uint_as_float(x[j2] << 16), i0[t] + 2 * j2);
+              take(__uint_as_float(x[j2] & 0xffff0000u), i0[t] + 2 * j2 + 1);
+            } else {
+              take(__half2float(__ushort_as_half((uint16_t)(x[j2] & 0xffffu))), i0[t] + 2 * j2);
+              take(__half2float(__ushort_as_half((uint16_t)(x[j2] >> 16))), i0[t] + 2 * j2 + 1);
             }
           }
         }
-      } else {
-        for (int q = tid; q < nrc * g.CE; q += NT) {
-          const int i = (int)s_cnt[q / g.CE] * g.CE + q % g.CE;
-          if (i < V) take(load_logit(zrow, g.dtype, i), i);
-        }
+      }
+    } else {
+      for (int q = tid; q < nrc * g.CE; q += NT) {
+        const int i = (int)s_cnt[q / g.CE] * g.CE + q % g.CE;
+        if (i < V) take(load_logit(zrow, g.dtype, i), i);
       }
     }
     __syncthreads();
@@ -567,44 +633,24 @@ __global__ void __launch_bounds__(NT, 2) lss_resolve_kernel(const RowArgs a, con
       if (tid == 0) a.defer_rows[atomicAdd(&a.counters[2], 1u)] = row;
       return;
     }
-    // Sort, merge equal codes, and take the max and the min-p key again: every value at or
-    // above the old cut is now present, and the exact cut is at least the old one.
-    {
-      const int np = next_pow2(nk);
-      for (int i = nk + tid; i < np; i += NT) G[i] = 0ull;
-      __syncthreads();
-      bitonic_sort(G, np, true);
-      __syncthreads();
-      uint64_t v[PER];
-      uint32_t keep = 0;
-#pragma unroll
-      for (int j = 0; j < PER; ++j) {
-        const int i = tid * PER + j;
-        v[j] = i < nk ? G[i] : 0ull;
-        if (i < nk && (i == 0 || G[i - 1] != v[j])) keep |= 1u << j;
-      }
-      uint32_t all;
-      const uint32_t at = block_excl_scan((uint32_t)__popc(keep), r32, all);
-      __syncthreads();
-      uint32_t o = at;
-#pragma unroll
-      for (int j = 0; j < PER; ++j)
-        if (keep & (1u << j)) G[o++] = v[j];
-      __syncthreads();
-      nk = (int)all;
-    }
-    my = key2f((uint32_t)(G[0] >> 32));
+    // Every value at or above the old cut is now present once, and the exact cut is at least
+    // the old one: the max, the min-p key and the k-th largest again.
+    uint32_t mk = 0u;
+    for (int i = tid; i < nk; i += NT) mk = max(mk, (uint32_t)(G[i] >> 32));
+    mk = block_allreduce(mk, MaxU32(), r32);
+    my = key2f(mk);
     const uint32_t Kmp2 = mp_on ? minp_key(my, mp) : KEY_FINITE_MIN;
-    uint32_t c2 = 0;
-    for (int i = tid; i < nk; i += NT) c2 += (uint32_t)(G[i] >> 32) >= Kmp2 ? 1u : 0u;
-    nk = (int)block_allreduce(c2, SumU32(), r32);
-    sorted = true;
+    cut = Kmp2;
+    nk = compact(nk, [&](uint64_t c) { return (uint32_t)(c >> 32) >= Kmp2; });
+    if (tk_on && k <= nk) cut = max(cut, kth_largest(nk, k));
   }
+  // The survivors of the cut, sorted (value desc, index asc) unless one warp takes them.
+  if (cut > Kmp) nk = compact(nk, [&](uint64_t c) { return (uint32_t)(c >> 32) >= cut; });
   const ResolveIn in{my, tk_on, k, tp > 0.0f && tp < 1.0f, tp, u, row, V};
   if (nk <= 32) {
     if (tid < 32) resolve_warp(tid < nk ? G[tid] : 0ull, nk, in, a, LSS_PATH_GATHER);
   } else {
-    resolve_block<FAST_CAP>(G, E, nk, in, a, rs, LSS_PATH_GATHER, sorted);
+    resolve_block<FAST_CAP>(G, E, nk, in, a, rs, LSS_PATH_GATHER);
   }
 }
 
