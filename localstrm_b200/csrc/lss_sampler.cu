@@ -649,6 +649,87 @@ size_t lss_shard_merge_workspace_bytes(int B) {
   return 256 + (((size_t)(B > 0 ? B : 1) * 4 + 255) & ~(size_t)255);
 }
 
+}  // extern "C"
+
+namespace lss {
+// Vocabulary-shard step as clusters (lss_shard_cluster_kernel): P CTAs per row, parts of about
+// 32 KB (64 KB at most, 16 CTAs at most), about 4K group maxima per row.  Returns false (and
+// launches nothing) when the shard row does not fit or no such cluster can be resident.
+template <int DT>
+static bool launch_shard_cluster(const void* logits, int64_t stride, int B, int Vs, int64_t voff, const float* T,
+                                 int K, unsigned char* rec, cudaStream_t st, cudaError_t& err) {
+  constexpr int es = DT == LSS_DTYPE_F32 ? 4 : 2;
+  const int P = (int)std::min<int64_t>(SC_MAXCL, std::max<int64_t>(1, ((int64_t)Vs * es + 32767) / 32768));
+  const int PS = round_up((Vs + P - 1) / P, 8);
+  if ((size_t)PS * es > (size_t)SC_PART_MAX) return false;
+  int L = 32;
+  while (L > 1 && (int64_t)P * (SC_NT / L) < 4LL * K) L >>= 1;
+  while (L < 32 && (int64_t)P * (SC_NT / L) > SC_GKMAX) L <<= 1;
+  if ((int64_t)P * (SC_NT / L) < K || (int64_t)P * (SC_NT / L) > SC_GKMAX) return false;
+  const size_t smem = sc_part_bytes(PS, es) + sizeof(ScCtl);
+  const size_t smem_max = (size_t)SC_PART_MAX + sizeof(ScCtl);
+  // Per device: attributes set, and per cluster size whether such clusters fit (-1 unknown).
+  static int attr_set[64] = {};
+  static int fits[64][SC_MAXCL + 1];
+  static bool fits_init = false;
+  const int dev = current_device();
+  {
+    std::lock_guard<std::mutex> lock(g_cfg_mu);
+    if (!fits_init) {
+      for (auto& d : fits)
+        for (int& f : d) f = -1;
+      fits_init = true;
+    }
+    if (!attr_set[dev]) {
+      err = cudaFuncSetAttribute(lss_shard_cluster_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem_max);
+      if (err == cudaSuccess)
+        err = cudaFuncSetAttribute(lss_shard_cluster_kernel<DT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (err != cudaSuccess) {
+        cudaGetLastError();
+        err = cudaSuccess;
+        return false;
+      }
+      attr_set[dev] = 1;
+    }
+    if (fits[dev][P] < 0) {
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3((unsigned)(P * 64), 1, 1);
+      cfg.blockDim = dim3(SC_NT, 1, 1);
+      cfg.dynamicSmemBytes = smem_max;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = (unsigned)P;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int nc = 0;
+      const cudaError_t e = cudaOccupancyMaxActiveClusters(&nc, lss_shard_cluster_kernel<DT>, &cfg);
+      if (e != cudaSuccess) cudaGetLastError();
+      fits[dev][P] = (e == cudaSuccess && nc > 0) ? 1 : 0;
+    }
+    if (!fits[dev][P]) return false;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(B * P), 1, 1);
+  cfg.blockDim = dim3(SC_NT, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = (unsigned)P;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  err = cudaLaunchKernelEx(&cfg, lss_shard_cluster_kernel<DT>, logits, stride, Vs, voff, T, K, PS, L, rec);
+  return true;
+}
+}  // namespace lss
+
+extern "C" {
+
 int lss_shard_topk(const void* logits, int dtype, int B, int Vs, int64_t row_stride, int64_t vocab_offset,
                    const float* temperature, int K, void* records_out, void* stream) {
   if (B < 0 || Vs < 1 || row_stride < Vs || vocab_offset < 0 || K < 1 || K > LSS_SHARD_MAX_K)
@@ -660,6 +741,29 @@ int lss_shard_topk(const void* logits, int dtype, int B, int Vs, int64_t row_str
     return LSS_ERR_INVALID_ARG;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   unsigned char* rec = reinterpret_cast<unsigned char*>(records_out);
+  {
+    cudaError_t e = cudaSuccess;
+    bool launched = false;
+    switch (dtype) {
+      case LSS_DTYPE_F32:
+        launched = launch_shard_cluster<LSS_DTYPE_F32>(logits, row_stride, B, Vs, vocab_offset, temperature, K, rec, st, e);
+        break;
+      case LSS_DTYPE_BF16:
+        launched = launch_shard_cluster<LSS_DTYPE_BF16>(logits, row_stride, B, Vs, vocab_offset, temperature, K, rec, st, e);
+        break;
+      default:
+        launched = launch_shard_cluster<LSS_DTYPE_F16>(logits, row_stride, B, Vs, vocab_offset, temperature, K, rec, st, e);
+        break;
+    }
+    if (launched) {
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        return LSS_ERR_CUDA;
+      }
+      return LSS_OK;
+    }
+  }
+  // Shard rows longer than 16 parts of 64 KB: one CTA per row, three passes.
   switch (dtype) {
     case LSS_DTYPE_F32:
       lss_shard_kernel<LSS_DTYPE_F32><<<B, NT, 0, st>>>(logits, row_stride, Vs, vocab_offset, temperature, K, rec);

@@ -224,6 +224,362 @@ __global__ void __launch_bounds__(NT) lss_shard_kernel(const void* logits, int64
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// K_SC (lss_shard_cluster_kernel): the same record in one pass over HBM.  A cluster of P CTAs
+// takes one row of the shard; CTA r stages the part [r PS, (r + 1) PS) of the row in its
+// shared memory with one bulk copy and reads it from there:
+//   1. the part's max of z and whether it holds NaN / +inf, and the max of every group of L
+//      lanes' values (the "group maxima");
+//   2. cluster barrier; every CTA reads the CTAs' maxima and all group maxima through
+//      distributed shared memory and takes F, the K-th largest group max: K groups reach F,
+//      so K values do, and every value among the row's K largest is at least F;
+//   3. each CTA adds exp(y - max) over its finite values and sends the values with
+//      y >= y(F) as codes to rank 0's candidate buffer (one remote atomic per warp);
+//   4. cluster barrier; rank 0 sorts the ~K candidates and writes the record.
+// With about 4K group maxima the candidates number little more than K.  A row with NaN / +inf
+// (or nothing finite) after scaling sends its argmax code (NaN first, lowest index) instead.
+// ---------------------------------------------------------------------------------------
+constexpr int SC_NT = NT;                 // threads per CTA (bitonic_sort works on NT threads)
+constexpr int SC_MAXCL = 16;              // CTAs per row at most
+constexpr int SC_CAP = SHARD_CAND;        // candidates rank 0 collects
+constexpr int SC_GKMAX = 2048;            // group maxima of a row at most
+constexpr int SC_PART_MAX = 64 * 1024;    // bytes of a part at most (64 values per thread)
+constexpr uint32_t SHARD_TIMEOUT = 4u;    // a bulk copy did not land in time
+
+struct ScCtl {
+  uint64_t bar;
+  uint32_t n;                   // rank 0: candidates sent
+  uint32_t zkey;                // this CTA's max key of z
+  uint32_t spec;                // this CTA saw NaN / +inf
+  uint32_t pad;
+  double psum[SC_MAXCL];        // rank 0: partial sums of exp(y - max), by rank
+  uint64_t best[SC_MAXCL];      // rank 0: argmax codes of a special row, by rank
+  uint32_t flags[SC_MAXCL];     // rank 0: flags, by rank
+  uint32_t bins[260];
+  uint32_t gk[SC_NT];           // this CTA's group maxima
+  uint32_t allk[SC_GKMAX];      // every group max of the row
+  uint64_t cand[SC_CAP];        // rank 0: candidates
+};
+
+// 2^x (PTX ex2.approx: relative error about 2^-22; -inf gives +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+__host__ __device__ constexpr size_t sc_part_bytes(int PS, int es) { return ((size_t)PS * es + 15) & ~(size_t)15; }
+
+// k-th largest of the u32 keys key(0 .. n-1) (1 <= k <= n): radix select, eight bits per pass,
+// down to bit `low` (0 for the exact key; 16 gives the largest multiple of 2^16 that at least k
+// keys reach, in two passes).  Whole CTA (NT threads); `bins` holds 258 words.
+template <class KeyAt>
+__device__ uint32_t block_kth_largest(KeyAt key_at, int n, int k, uint32_t* bins, int low = 0) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  uint32_t prefix = 0u, mask = 0u;
+  for (int shift = 24; shift >= low; shift -= 8) {
+    for (int b = tid; b < 256; b += NT) bins[b] = 0u;
+    __syncthreads();
+    for (int i = tid; i < n; i += NT) {
+      const uint32_t key = key_at(i);
+      if ((key & mask) == prefix) atomicAdd(&bins[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (tid < 32) {
+      // Lane l holds bins 255 - 8l .. 248 - 8l (largest digits first).
+      uint32_t c8[8], loc = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        c8[q] = bins[255 - (8 * lane + q)];
+        loc += c8[q];
+      }
+      uint32_t incl = loc;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const unsigned hit = __ballot_sync(0xffffffffu, incl >= (uint32_t)k);
+      const int L = hit ? __ffs(hit) - 1 : 31;
+      if (lane == L) {
+        uint32_t acc = incl - loc;
+        int d = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (acc + c8[q] >= (uint32_t)k) {
+            d = 255 - (8 * lane + q);
+            break;
+          }
+          acc += c8[q];
+        }
+        bins[256] = (uint32_t)d;
+        bins[257] = acc;  // keys with a larger digit
+      }
+    }
+    __syncthreads();
+    prefix |= bins[256] << shift;
+    mask |= 255u << shift;
+    k -= (int)bins[257];
+    __syncthreads();
+  }
+  return prefix;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(SC_NT) lss_shard_cluster_kernel(const void* logits, int64_t row_stride, int Vs,
+                                                                  int64_t voff, const float* temperature, int K,
+                                                                  int PS, int L, unsigned char* rec) {
+  constexpr int ES = DT == LSS_DTYPE_F32 ? 4 : 2;
+  constexpr int VE = 16 / ES;             // values per 16-byte vector
+  constexpr int MAXV = SC_PART_MAX / 16 / SC_NT;  // vectors per thread at most (8)
+  extern __shared__ __align__(128) unsigned char scm[];
+  cg::cluster_group cl = cg::this_cluster();
+  const int P = (int)cl.num_blocks();
+  const int me = (int)cl.block_rank();
+  const int row = blockIdx.x / P;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  unsigned char* part = scm;
+  ScCtl& c = *reinterpret_cast<ScCtl*>(scm + sc_part_bytes(PS, ES));
+  __shared__ uint32_t r32[NWARP];
+  __shared__ uint64_t r64[NWARP];
+  __shared__ double rd[NWARP];
+  const int lo = me * PS;
+  const int n = max(0, min(Vs, lo + PS) - lo);
+  const char* src = reinterpret_cast<const char*>(logits) + ((int64_t)row * row_stride + lo) * ES;
+  const float T = temperature[row];
+  const bool greedy = T <= 0.0f;  // codes of the raw values (their order is all a greedy row needs)
+  auto y_of = [&](float z) -> float { return greedy ? z : __fdiv_rn(z, T); };
+  // ---- the part into shared memory: one bulk copy of its 16-byte aligned body, plain loads
+  // for the rest (a misaligned row, a ragged tail)
+  const uint32_t nb = (reinterpret_cast<uintptr_t>(src) & 15) == 0 ? (uint32_t)((n * ES) & ~15) : 0u;
+  if (tid == 0) {
+    c.n = 0u;
+    c.pad = 0u;
+    mbar_init(&c.bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    mbar_expect_tx(&c.bar, nb);
+    if (nb > 0) bulk_g2s(part, src, nb, &c.bar);
+  }
+  for (int i = (int)nb / ES + tid; i < n; i += SC_NT) {
+    if (ES == 4) reinterpret_cast<float*>(part)[i] = reinterpret_cast<const float*>(src)[i];
+    else reinterpret_cast<uint16_t*>(part)[i] = reinterpret_cast<const uint16_t*>(src)[i];
+  }
+  uint32_t myflags = 0u;
+  if (!mbar_wait_bounded(&c.bar, 0)) myflags |= SHARD_TIMEOUT;
+  __syncthreads();
+  // Values of vector q of the part (elements q VE .. q VE + VE - 1), widened.
+  auto vec = [&](int q, float* x) {
+    const uint4 r = reinterpret_cast<const uint4*>(part)[q];
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (DT == LSS_DTYPE_F32) {
+        x[j] = __uint_as_float(w[j]);
+      } else if (DT == LSS_DTYPE_BF16) {
+        x[2 * j] = __uint_as_float(w[j] << 16);
+        x[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+      } else {
+        x[2 * j] = __half2float(__ushort_as_half((uint16_t)(w[j] & 0xffffu)));
+        x[2 * j + 1] = __half2float(__ushort_as_half((uint16_t)(w[j] >> 16)));
+      }
+    }
+  };
+  const int nvec = (n + VE - 1) / VE;
+  const int nfull = n / VE;  // vectors whose values all belong to the part
+  // ---- 1. maxima: this thread's vectors are q = tid + v NT.  fmaxf passes over NaN, which
+  // the flag records (+inf shows up as the max).
+  float tmax = -INFINITY;
+  bool spec = false;
+#pragma unroll
+  for (int v = 0; v < MAXV; ++v) {
+    const int q = tid + v * SC_NT;
+    if (q < nvec) {
+      float x[VE];
+      vec(q, x);
+      const int lim = q < nfull ? VE : n - q * VE;
+#pragma unroll
+      for (int j = 0; j < VE; ++j) {
+        if (j < lim) {
+          tmax = fmaxf(tmax, x[j]);
+          spec |= x[j] != x[j];
+        }
+      }
+    }
+  }
+  const uint32_t tkey = f2key(tmax);
+  uint32_t gkey = tkey;
+  for (int o = 1; o < L; o <<= 1) gkey = max(gkey, __shfl_xor_sync(0xffffffffu, gkey, o));
+  const int G1 = SC_NT / L;  // groups per CTA
+  if ((lane & (L - 1)) == 0) c.gk[warp * (32 / L) + lane / L] = gkey;
+  // The part's max key and NaN / +inf flag in one reduction (flag above the key).
+  const uint64_t cm = block_allreduce(((uint64_t)(spec ? 1u : 0u) << 32) | tkey, MaxU64(), r64);
+  if (tid == 0) {
+    c.zkey = (uint32_t)cm;
+    c.spec = (uint32_t)(cm >> 32);
+  }
+  cl.sync();  // 2. every CTA's maxima are visible cluster-wide
+  uint64_t rm = 0ull;
+  if (tid < P) {
+    const ScCtl* rc = cl.map_shared_rank(&c, tid);
+    rm = ((uint64_t)rc->spec << 32) | rc->zkey;
+  }
+  rm = block_allreduce(rm, MaxU64(), r64);
+  const uint32_t zk = (uint32_t)rm, sp = (uint32_t)(rm >> 32);
+  const int GK = P * G1;
+  for (int t = tid; t < GK; t += SC_NT) c.allk[t] = cl.map_shared_rank(&c, t / G1)->gk[t % G1];
+  // Max of y: NaN when the row holds a NaN; +inf when it holds +inf (or the division
+  // overflows); -inf when nothing is finite (zk then is the key of -inf or 0).
+  float my;
+  if (sp) {
+    my = INFINITY;  // refined below: NaN if any NaN
+  } else {
+    my = zk >= KEY_FINITE_MIN ? y_of(key2f(zk)) : -INFINITY;
+  }
+  const bool special = sp || !(my > -INFINITY && my < INFINITY);
+  ScCtl* c0 = cl.map_shared_rank(&c, 0);
+  unsigned char* r = rec + (size_t)row * shard_record_bytes(K);
+  uint64_t* codes = reinterpret_cast<uint64_t*>(r);
+  uint32_t* tail = reinterpret_cast<uint32_t*>(r + (size_t)K * 8);
+  if (special) {
+    // The NaN guard's argmax over the row's y (NaN first, lowest index), and whether a NaN is
+    // in the row (then the max is NaN).
+    uint64_t best = 0;
+    bool nan = false;
+    for (int i = tid; i < n; i += SC_NT) {
+      const float z = DT == LSS_DTYPE_F32 ? reinterpret_cast<const float*>(part)[i]
+                      : DT == LSS_DTYPE_BF16
+                          ? __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(part)[i] << 16)
+                          : __half2float(__ushort_as_half(reinterpret_cast<const uint16_t*>(part)[i]));
+      const float y = y_of(z);
+      nan |= !(y == y);
+      best = max(best, argmax_code(y, (int)(voff + lo + i)));
+    }
+    best = block_allreduce(best, MaxU64(), r64);
+    const uint32_t anynan = block_allreduce(nan ? 1u : 0u, OrU32(), r32);
+    if (tid == 0) {
+      c0->best[me] = best;
+      c0->flags[me] = myflags | (anynan ? 0x80000000u : 0u);
+    }
+    cl.sync();  // 4. rank 0 has every part's argmax
+    if ((myflags & SHARD_TIMEOUT) && tid == 0) mbar_wait_bounded(&c.bar, 0);
+    if (me == 0) {
+      uint64_t b = 0;
+      uint32_t fl = 0;
+      for (int q = 0; q < P; ++q) {
+        b = max(b, c.best[q]);
+        fl |= c.flags[q];
+      }
+      const float m = (fl & 0x80000000u) ? __int_as_float(0x7fc00000) : my;
+      for (int i = tid; i < K; i += SC_NT) codes[i] = i == 0 ? b : 0ull;
+      if (tid == 0) {
+        tail[0] = __float_as_uint(m);
+        tail[1] = __float_as_uint(m == -INFINITY ? 0.0f : __int_as_float(0x7fc00000));
+        tail[2] = (m == -INFINITY ? 0u : SHARD_SPECIAL) | (fl & SHARD_TIMEOUT);
+        tail[3] = 1u;
+      }
+    }
+    return;
+  }
+  __syncthreads();  // allk complete
+  // F: a key at most the K-th largest group max, to within 2^-7 of its value (the top 16 bits
+  // of the key: sign, exponent, seven mantissa bits); at least K groups reach it.  No bound
+  // when fewer than K groups hold a finite value.
+  const uint32_t F = block_kth_largest([&](int i) { return c.allk[i]; }, GK, K, c.bins, 16);
+  const float yF = F >= KEY_FINITE_MIN ? y_of(key2f(F)) : -INFINITY;
+  // Values below zlow cannot reach y(F); only the others are divided exactly.
+  const float zlow = (yF == -INFINITY) ? -INFINITY : (greedy ? yF : z_floor_for(yF, T));
+  const float zmax = key2f(zk);
+  const float invT = greedy ? 1.0f : __frcp_rn(T);
+  // ---- 3. sum of exp(y - max) over the finite values, as 2^((z - zmax) log2(e) / T) (within a
+  // few ulp of the exact terms; per vector in f32, then in f64), and the candidates y >= y(F)
+  const float c2 = __fmul_rn(invT, 1.4426950408889634f);
+  using Mask = unsigned long long;
+  Mask m = 0;
+  double sl = 0.0;
+  int cnt = 0;
+#pragma unroll
+  for (int v = 0; v < MAXV; ++v) {
+    const int q = tid + v * SC_NT;
+    if (q < nvec) {
+      float x[VE];
+      vec(q, x);
+      const int lim = q < nfull ? VE : n - q * VE;
+      float e[VE];
+#pragma unroll
+      for (int j = 0; j < VE; ++j) {
+        e[j] = 0.0f;
+        if (j < lim) {
+          e[j] = ex2_approx(__fmul_rn(__fsub_rn(x[j], zmax), c2));
+          if (x[j] >= zlow && x[j] > -INFINITY) {
+            const float y = y_of(x[j]);
+            if (y >= yF && y > -INFINITY) {
+              m |= (Mask)1 << (v * VE + j);
+              ++cnt;
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int w2 = VE / 2; w2 >= 1; w2 /= 2)
+#pragma unroll
+        for (int j = 0; j < w2; ++j) e[j] += e[j + w2];
+      sl += (double)e[0];
+    }
+  }
+  uint32_t incl = (uint32_t)cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  uint32_t base = 0;
+  if (lane == 31 && incl) base = atomicAdd(&c0->n, incl);
+  base = __shfl_sync(0xffffffffu, base, 31) + incl - (uint32_t)cnt;
+  while (m) {
+    const int b = __ffsll((long long)m) - 1;
+    m &= m - 1;
+    const int v = b / VE, j = b % VE;
+    const int i = (tid + v * SC_NT) * VE + j;
+    float x[VE];
+    vec(tid + v * SC_NT, x);
+    if (base < (uint32_t)SC_CAP)
+      c0->cand[base] = ((uint64_t)f2key(y_of(x[j])) << 32) | (uint32_t)(~(uint32_t)(voff + lo + i));
+    ++base;
+  }
+  const double se = block_allreduce(sl, SumD(), rd);
+  if (tid == 0) {
+    c0->psum[me] = se;
+    c0->flags[me] = myflags;
+  }
+  cl.sync();  // 4. rank 0 holds every candidate and partial sum
+  // After a bulk copy gave up, wait (bounded) once more for it before the memory is released.
+  if ((myflags & SHARD_TIMEOUT) && tid == 0) mbar_wait_bounded(&c.bar, 0);
+  if (me != 0) return;
+  const uint32_t n_all = c.n;
+  const int nc = (int)min(n_all, (uint32_t)SC_CAP);
+  const int np = next_pow2(nc > 1 ? nc : 1);
+  for (int i = nc + tid; i < np; i += SC_NT) c.cand[i] = 0ull;
+  __syncthreads();
+  bitonic_sort(c.cand, np, true);
+  __syncthreads();
+  for (int i = tid; i < K; i += SC_NT) codes[i] = i < nc ? c.cand[i] : 0ull;
+  if (tid == 0) {
+    double S = 0.0;
+    uint32_t fl = 0;
+    for (int q = 0; q < P; ++q) {
+      S += c.psum[q];
+      fl |= c.flags[q];
+    }
+    tail[0] = __float_as_uint(my);
+    tail[1] = __float_as_uint((float)S);
+    tail[2] = (n_all > (uint32_t)SC_CAP ? SHARD_OVER : 0u) | (fl & SHARD_TIMEOUT);
+    tail[3] = (uint32_t)min(nc, K);
+  }
+}
+
 // The records are gathered shard-major: shard s, row b at (s * B + b) * shard_record_bytes(K).
 __global__ void __launch_bounds__(NT) lss_merge_kernel(const unsigned char* recs, int nshards, int B, int K,
                                                        const RowArgs a) {
@@ -277,10 +633,12 @@ __global__ void __launch_bounds__(NT) lss_merge_kernel(const unsigned char* recs
       a.tokens[row] = (int32_t)(~(uint32_t)best);
       a.row_path[row] = T <= 0.0f ? LSS_PATH_GREEDY : LSS_PATH_SPECIAL;
       if (s_flags & SHARD_OVER) atomicOr(a.err, LSS_FLAG_INTERNAL);
+      if (s_flags & SHARD_TIMEOUT) atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
     }
     return;
   }
   if (tid == 0 && (s_flags & SHARD_OVER)) atomicOr(a.err, LSS_FLAG_INTERNAL);
+  if (tid == 0 && (s_flags & SHARD_TIMEOUT)) atomicOr(a.err, LSS_FLAG_TMA_TIMEOUT);
   const float tp = a.top_p[row];
   const ResolveIn in{my, true, K, tp > 0.0f && tp < 1.0f, tp, a.uniforms[row], row, a.V};
   const RedScratch rs{r64, rd, r32, ri};

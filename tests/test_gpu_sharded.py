@@ -21,6 +21,9 @@ pytestmark = pytest.mark.gpu
 needs_cuda = pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")
 
 
+DT_CODE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+
 def _gpu_records(lib, x, w, n, K):
     rb = lib.lss_shard_record_bytes(K)
     T = torch.from_numpy(w.temperature).cuda()
@@ -29,8 +32,9 @@ def _gpu_records(lib, x, w, n, K):
         off, stop = shard_vocab(w.V, n, s)
         rec = torch.empty(w.B * rb, dtype=torch.uint8, device="cuda")
         view = x[:, off:stop]
-        _lib.check("lss_shard_topk", lib.lss_shard_topk(view.data_ptr(), 0, w.B, stop - off, view.stride(0), off,
-                                                         T.data_ptr(), K, rec.data_ptr(), None))
+        _lib.check("lss_shard_topk", lib.lss_shard_topk(view.data_ptr(), DT_CODE[x.dtype], w.B, stop - off,
+                                                         view.stride(0), off, T.data_ptr(), K, rec.data_ptr(),
+                                                         None))
         recs.append(rec)
     return torch.cat(recs), T
 
@@ -111,6 +115,31 @@ def test_config5_full_size_emulated_shards(n):
         assert int(tok[b]) == own or P.draw_is_boundary(np.where(kept[b], probs[b], 0), float(w.uniforms[b])), b
         if int(tok[b]) != res.token:
             assert P.draw_is_boundary(res.probs, float(w.uniforms[b])), (b, int(tok[b]), res.token)
+
+
+@needs_cuda
+@pytest.mark.parametrize("dtype,V,n,K", [("bf16", 64_000, 2, 64), ("f16", 64_000, 8, 64), ("f32", 64_001, 2, 64),
+                                         ("f32", 300_000, 1, 256), ("bf16", 40_000, 4, 16)])
+def test_vocab_shard_records_dtypes_and_layouts(dtype, V, n, K):
+    """Shard records of 16-bit logits (compared with the oracle on the widened values), of
+    shards that start off a 16-byte boundary (V odd), of a long shard row with K = 256 and of
+    a small K: codes, max, flags and count byte for byte, the sum within 1e-5."""
+    lib = _lib.load()
+    w = wl.config5(seed=13, B=12, V=V)
+    w.logits = wl.round_to_dtype(w.logits, dtype)
+    w.temperature[3] = 0.0  # a greedy row: codes of the raw values
+    tdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[dtype]
+    x = torch.from_numpy(w.logits).to(tdt).cuda()
+    gathered, T = _gpu_records(lib, x, w, n, K)
+    rb = lib.lss_shard_record_bytes(K)
+    g = gathered.cpu().numpy().reshape(n, w.B, rb)
+    for s in range(n):
+        off, stop = shard_vocab(w.V, n, s)
+        ref = OS.shard_records(w.logits[:, off:stop], off, w.temperature, K).reshape(w.B, rb)
+        assert np.array_equal(g[s, :, :8 * K + 4], ref[:, :8 * K + 4]), s          # codes, max
+        assert np.array_equal(g[s, :, 8 * K + 8:], ref[:, 8 * K + 8:]), s          # flags, count
+        se, se_ref = g[s, :, 8 * K + 4:8 * K + 8].view(np.float32), ref[:, 8 * K + 4:8 * K + 8].view(np.float32)
+        assert np.allclose(se, se_ref, rtol=1e-5), s
 
 
 @needs_cuda
