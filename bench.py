@@ -40,7 +40,7 @@ V = 151_936
 L2_BYTES = 126e6
 TORCH_DT = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
 DT_CODE = {"f32": 0, "bf16": 1, "f16": 2}
-WORKLOADS = ("headline", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5")
+WORKLOADS = ("headline", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "greedy")
 DESC = {
     "headline": "headline: B=256 rows/GPU, V=151936 f32 logits, T0.7 p0.95 mp0.05 rep1.1 freq0.3 pres0.2, H=2048",
     "cfg1": "config 1: B=8 rows/GPU, V=151936 f32, 2 greedy + 6 T0.8/k50/p0.9",
@@ -48,6 +48,7 @@ DESC = {
     "cfg3": "config 3: B=256 rows/GPU, V=128256 f32, T0.7 p0.95 mp0.05 rep1.1 freq0.3 pres0.2, H=2048",
     "cfg4": "config 4: B=1024 rows split over the GPUs, V=151936 bf16, every feature on",
     "cfg5": "config 5: B=128, V=256000 f32 split by columns over the GPUs, T1.0 top-k 64 (records) p0.9",
+    "greedy": "greedy seam: B=256 rows/GPU, V=151936 f32 logits (headline rows), argmax of every row",
 }
 
 
@@ -212,6 +213,10 @@ def make_workload(rank: int, world: int = 1, name: str = "headline", strong: boo
             a, b = shard_rows(full.B, world, rank)
             return _row_block(full, a, b)
         return wl.headline(seed=rank, B=B_PER_GPU, V=V)
+    if name == "greedy":
+        w = wl.headline(seed=rank, B=B_PER_GPU, V=V)
+        w.temperature[:] = 0.0
+        return w
     if name == "cfg4":
         full = wl.config4(seed=0)
         a, b = shard_rows(full.B, world, rank)
@@ -608,9 +613,75 @@ def run_vocab(args, rank: int, world: int, local_rank: int):
             "data": "synthetic (seeded; cfg5)",
             "config": vocab_config(args, w, world), "records_bytes_per_rank": B * rb,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "kernel": "lss_shard_kernel",
+                         "frac": achieved / peak, "traffic": None, "kernel": "lss_shard_cluster_kernel",
                          "peak_source": peak_kind, "algorithmic_bytes_per_launch": alg, "kernel_ms": kern_ms},
             "clocks": clk, "e2e": None, "cpu_baseline": cpu, "gpu_launches": 2 * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def run_greedy(args, rank: int, world: int, local_rank: int):
+    """The engine's all-greedy seam (llm_engine.py:1139-1141, torch.argmax of the batch): one
+    lss_argmax per step over each rank's own 256 headline rows, timed with events."""
+    from localstrm_b200 import _lib
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+    w = make_workload(rank, world, "headline")
+    B = w.B
+    host = torch.from_numpy(w.logits).pin_memory()
+    nbuf = n_buffers(host.numel() * 4)
+    bufs = [host.to(dev) for _ in range(nbuf)]
+    tok = torch.empty(B, dtype=torch.int32, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def step(i):
+        x = bufs[i % nbuf]
+        _lib.check("lss_argmax", lib.lss_argmax(x.data_ptr(), 0, B, w.V, x.stride(0), tok.data_ptr(),
+                                                st.cuda_stream))
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(args.steps):
+        step(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    got = tok.cpu().numpy()
+    ref = np.argmax(w.logits[:, :], axis=1)  # no NaN in these rows
+    assert np.array_equal(got, ref.astype(np.int32)), "argmax mismatch"
+    alg = B * w.V * 4 + B * 4
+    peak, peak_kind = peaks()
+    achieved = alg / (ms / args.steps / 1000.0) / 1e9
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": B * world * args.steps / (ms / 1000.0), "unit": "rows/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; config 3 distribution at V=151,936)",
+            "config": {"workload": DESC["greedy"], "global_batch": B * world, "rows_per_gpu": B, "vocab": w.V,
+                       "parallelism": f"rows{world}" if world > 1 else "single",
+                       "l2": f"{nbuf} rotating input buffers of {host.numel() * 4 / 1e6:.1f} MB"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "kernel": "lss_argmax_kernel",
+                         "peak_source": peak_kind, "algorithmic_bytes_per_launch": alg,
+                         "kernel_ms": ms / args.steps},
+            "clocks": clk, "e2e": None, "cpu_baseline": None, "gpu_launches": args.steps,
         }
         print(json.dumps(line), flush=True)
 
@@ -650,6 +721,8 @@ def main():
     try:
         if args.workload == "cfg5":
             run_vocab(args, rank, world, local_rank)
+        elif args.workload == "greedy":
+            run_greedy(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

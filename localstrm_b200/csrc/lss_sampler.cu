@@ -59,26 +59,38 @@ __global__ void __launch_bounds__(NT) lss_argmax_kernel(const void* logits, int6
   if ((reinterpret_cast<uintptr_t>(g0) & 15) != 0) head = n;  // unaligned rows: scalar path
   const int nvec = (n - head) / VE;
   for (int i = threadIdx.x; i < head; i += NT) best = max(best, argmax_code(val(i), lo + i));
-  for (int q = threadIdx.x; q < nvec; q += NT) {
-    uint4 raw = __ldg(reinterpret_cast<const uint4*>(g0) + q);
-    const int i = lo + q * VE;
-    uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-    if (DT == LSS_DTYPE_F32) {
+  // Eight 16-byte loads per thread requested before any is used.
+  constexpr int U = 8;
+  for (int q0 = 0; q0 < nvec; q0 += U * NT) {
+    uint4 raw[U];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) best = max(best, argmax_code(__uint_as_float(w[j]), i + j));
-    } else {
+    for (int u = 0; u < U; ++u) {
+      const int q = q0 + u * NT + (int)threadIdx.x;
+      raw[u] = q < nvec ? __ldg(reinterpret_cast<const uint4*>(g0) + q) : make_uint4(0u, 0u, 0u, 0u);
+    }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float a0, a1;
-        if (DT == LSS_DTYPE_BF16) {
-          a0 = __uint_as_float(w[j] << 16);
-          a1 = __uint_as_float(w[j] & 0xffff0000u);
-        } else {
-          a0 = __half2float(__ushort_as_half((uint16_t)(w[j] & 0xffffu)));
-          a1 = __half2float(__ushort_as_half((uint16_t)(w[j] >> 16)));
+    for (int u = 0; u < U; ++u) {
+      const int q = q0 + u * NT + (int)threadIdx.x;
+      if (q >= nvec) break;
+      const int i = lo + q * VE;
+      const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+      if (DT == LSS_DTYPE_F32) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) best = max(best, argmax_code(__uint_as_float(w[j]), i + j));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float a0, a1;
+          if (DT == LSS_DTYPE_BF16) {
+            a0 = __uint_as_float(w[j] << 16);
+            a1 = __uint_as_float(w[j] & 0xffff0000u);
+          } else {
+            a0 = __half2float(__ushort_as_half((uint16_t)(w[j] & 0xffffu)));
+            a1 = __half2float(__ushort_as_half((uint16_t)(w[j] >> 16)));
+          }
+          best = max(best, argmax_code(a0, i + 2 * j));
+          best = max(best, argmax_code(a1, i + 2 * j + 1));
         }
-        best = max(best, argmax_code(a0, i + 2 * j));
-        best = max(best, argmax_code(a1, i + 2 * j + 1));
       }
     }
   }
