@@ -325,6 +325,61 @@ __device__ __forceinline__ uint64_t warp_sort(uint64_t v, bool descending) {
   return v;
 }
 
+// k-th largest of the u32 keys key(0 .. n-1) (1 <= k <= n): radix select, eight bits per pass,
+// down to bit `low` (0 for the exact key; 16 gives the largest multiple of 2^16 that at least k
+// keys reach, in two passes).  Whole CTA (NT threads); `bins` holds 258 words.
+template <class KeyAt>
+__device__ uint32_t block_kth_largest(KeyAt key_at, int n, int k, uint32_t* bins, int low = 0) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  uint32_t prefix = 0u, mask = 0u;
+  for (int shift = 24; shift >= low; shift -= 8) {
+    for (int b = tid; b < 256; b += NT) bins[b] = 0u;
+    __syncthreads();
+    for (int i = tid; i < n; i += NT) {
+      const uint32_t key = key_at(i);
+      if ((key & mask) == prefix) atomicAdd(&bins[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (tid < 32) {
+      // Lane l holds bins 255 - 8l .. 248 - 8l (largest digits first).
+      uint32_t c8[8], loc = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        c8[q] = bins[255 - (8 * lane + q)];
+        loc += c8[q];
+      }
+      uint32_t incl = loc;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const unsigned hit = __ballot_sync(0xffffffffu, incl >= (uint32_t)k);
+      const int L = hit ? __ffs(hit) - 1 : 31;
+      if (lane == L) {
+        uint32_t acc = incl - loc;
+        int d = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (acc + c8[q] >= (uint32_t)k) {
+            d = 255 - (8 * lane + q);
+            break;
+          }
+          acc += c8[q];
+        }
+        bins[256] = (uint32_t)d;
+        bins[257] = acc;  // keys with a larger digit
+      }
+    }
+    __syncthreads();
+    prefix |= bins[256] << shift;
+    mask |= 255u << shift;
+    k -= (int)bins[257];
+    __syncthreads();
+  }
+  return prefix;
+}
+
 // Smallest key K with exp(key2f(K) - m) >= mp (min-p keeps y with key >= K).
 __device__ __forceinline__ uint32_t minp_key(float m, float mp) {
   const uint32_t hiK = f2key(m);

@@ -29,6 +29,7 @@
 #include "lss_resolve.cuh"
 #include "lss_slow.cuh"
 #include "lss_shard.cuh"
+#include "lss_row.cuh"
 
 namespace lss {
 
@@ -309,6 +310,40 @@ static cudaError_t launch_clusters(K kern, const RowArgs& a, int CL, int ncluste
   return launch_pdl(kern, (unsigned)(nclusters * CL), (unsigned)NT, (size_t)smem, CL, st, a);
 }
 
+// K3 over the deferred-row list (programmatic dependent launch after the kernel before it).
+template <int DT>
+static cudaError_t launch_slow(const RowArgs& ra, const Plan& pl, int B, cudaStream_t st) {
+  cudaError_t e = cudaSuccess;
+  int ncs = 0;
+  switch (pl.CL) {
+    case 1: {
+      static KernelCfg c{};
+      e = prepare_cluster_kernel(lss_slow_kernel<1, DT>, c, 1, pl.slow_smem, ncs);
+      if (e == cudaSuccess) e = launch_clusters(lss_slow_kernel<1, DT>, ra, 1, std::min(ncs, B), pl.slow_smem, st);
+      break;
+    }
+    case 2: {
+      static KernelCfg c{};
+      e = prepare_cluster_kernel(lss_slow_kernel<2, DT>, c, 2, pl.slow_smem, ncs);
+      if (e == cudaSuccess) e = launch_clusters(lss_slow_kernel<2, DT>, ra, 2, std::min(ncs, B), pl.slow_smem, st);
+      break;
+    }
+    case 4: {
+      static KernelCfg c{};
+      e = prepare_cluster_kernel(lss_slow_kernel<4, DT>, c, 4, pl.slow_smem, ncs);
+      if (e == cudaSuccess) e = launch_clusters(lss_slow_kernel<4, DT>, ra, 4, std::min(ncs, B), pl.slow_smem, st);
+      break;
+    }
+    default: {
+      static KernelCfg c{};
+      e = prepare_cluster_kernel(lss_slow_kernel<8, DT>, c, 8, pl.slow_smem, ncs);
+      if (e == cudaSuccess) e = launch_clusters(lss_slow_kernel<8, DT>, ra, 8, std::min(ncs, B), pl.slow_smem, st);
+      break;
+    }
+  }
+  return e;
+}
+
 // K1 (streaming pass), K2 (resolve, one CTA per row), K3 (second kernel over the deferred list).
 template <int DT>
 static cudaError_t launch_rows(StreamArgs sa, const RowArgs& ra, GatherArgs ga, const Plan& pl, int B,
@@ -338,34 +373,76 @@ static cudaError_t launch_rows(StreamArgs sa, const RowArgs& ra, GatherArgs ga, 
   }
   e = launch_pdl(lss_resolve_kernel, (unsigned)B, (unsigned)NT, (size_t)resolve_smem_bytes(), 1, st, ra, ga);
   if (e != cudaSuccess) return e;
-  int ncs = 0;
-  switch (pl.CL) {
-    case 1: {
-      static KernelCfg c{};
-      e = prepare_cluster_kernel(lss_slow_kernel<1, DT>, c, 1, pl.slow_smem, ncs);
-      if (e == cudaSuccess) e = launch_clusters(lss_slow_kernel<1, DT>, ra, 1, std::min(ncs, B), pl.slow_smem, st);
-      break;
+  return launch_slow<DT>(ra, pl, B, st);
+}
+
+// The latency path for batches of up to RW_MAXB rows: lss_row_kernel (one cluster of up to 16
+// CTAs per row, an ordinary launch) then K3 for the rows it leaves.  Returns false (launching
+// nothing) when the row does not fit the path or such clusters cannot be resident.
+template <int DT>
+static bool launch_row_path(const RowArgs& ra, const Plan& pl, int B, int V, cudaStream_t st, cudaError_t& err) {
+  constexpr int es = DT == LSS_DTYPE_F32 ? 4 : 2;
+  const int CL = (int)std::min<int64_t>(RW_MAXCL, std::max<int64_t>(1, ((int64_t)V + 9599) / 9600));
+  const int TS = round_up((V + CL - 1) / CL, 8);
+  if (B < 1 || B > RW_MAXB || TS > RW_TILE_MAX) return false;
+  const size_t smem = rw_smem_bytes(TS, es);
+  static int attr_set[64] = {};
+  static int fits[64][RW_MAXCL + 1];
+  static bool fits_init = false;
+  const int dev = current_device();
+  {
+    std::lock_guard<std::mutex> lock(g_cfg_mu);
+    if (!fits_init) {
+      for (auto& d : fits)
+        for (int& f : d) f = -1;
+      fits_init = true;
     }
-    case 2: {
-      static KernelCfg c{};
-      e = prepare_cluster_kernel(lss_slow_kernel<2, DT>, c, 2, pl.slow_smem, ncs);
-      if (e == cudaSuccess) e = launch_clusters(lss_slow_kernel<2, DT>, ra, 2, std::min(ncs, B), pl.slow_smem, st);
-      break;
+    if (!attr_set[dev]) {
+      err = cudaFuncSetAttribute(lss_row_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)rw_smem_bytes(RW_TILE_MAX, es));
+      if (err == cudaSuccess)
+        err = cudaFuncSetAttribute(lss_row_kernel<DT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (err != cudaSuccess) {
+        cudaGetLastError();
+        err = cudaSuccess;
+        return false;
+      }
+      attr_set[dev] = 1;
     }
-    case 4: {
-      static KernelCfg c{};
-      e = prepare_cluster_kernel(lss_slow_kernel<4, DT>, c, 4, pl.slow_smem, ncs);
-      if (e == cudaSuccess) e = launch_clusters(lss_slow_kernel<4, DT>, ra, 4, std::min(ncs, B), pl.slow_smem, st);
-      break;
+    if (fits[dev][CL] < 0) {
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3((unsigned)(CL * RW_MAXB), 1, 1);
+      cfg.blockDim = dim3(NT, 1, 1);
+      cfg.dynamicSmemBytes = rw_smem_bytes(RW_TILE_MAX, es);
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = (unsigned)CL;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int nc = 0;
+      const cudaError_t e = cudaOccupancyMaxActiveClusters(&nc, lss_row_kernel<DT>, &cfg);
+      if (e != cudaSuccess) cudaGetLastError();
+      fits[dev][CL] = (e == cudaSuccess && nc >= RW_MAXB) ? 1 : 0;
     }
-    default: {
-      static KernelCfg c{};
-      e = prepare_cluster_kernel(lss_slow_kernel<8, DT>, c, 8, pl.slow_smem, ncs);
-      if (e == cudaSuccess) e = launch_clusters(lss_slow_kernel<8, DT>, ra, 8, std::min(ncs, B), pl.slow_smem, st);
-      break;
-    }
+    if (!fits[dev][CL]) return false;
   }
-  return e;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(B * CL), 1, 1);
+  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = (unsigned)CL;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  err = cudaLaunchKernelEx(&cfg, lss_row_kernel<DT>, ra, TS);
+  if (err == cudaSuccess) err = launch_slow<DT>(ra, pl, B, st);
+  return true;
 }
 
 template <int CL, int DT>
@@ -538,6 +615,23 @@ static int sample_rows(const void* logits, int dtype, int B, int V, int64_t row_
   ga.cmax = sa.cmax;
   ga.dtype = dtype;
   cudaError_t e;
+  // Batches of a few rows take the latency path (one cluster kernel per call, then K3).
+  if (!scan_only && B <= RW_MAXB) {
+    bool done = false;
+    e = cudaSuccess;
+    switch (dtype) {
+      case LSS_DTYPE_F32: done = launch_row_path<LSS_DTYPE_F32>(a, pl, B, V, st, e); break;
+      case LSS_DTYPE_BF16: done = launch_row_path<LSS_DTYPE_BF16>(a, pl, B, V, st, e); break;
+      default: done = launch_row_path<LSS_DTYPE_F16>(a, pl, B, V, st, e); break;
+    }
+    if (done) {
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        return LSS_ERR_CUDA;
+      }
+      return LSS_OK;
+    }
+  }
   switch (dtype) {
     case LSS_DTYPE_F32: e = launch_rows<LSS_DTYPE_F32>(sa, a, ga, pl, B, st, scan_only); break;
     case LSS_DTYPE_BF16: e = launch_rows<LSS_DTYPE_BF16>(sa, a, ga, pl, B, st, scan_only); break;
@@ -664,14 +758,15 @@ size_t lss_shard_merge_workspace_bytes(int B) {
 }  // extern "C"
 
 namespace lss {
-// Vocabulary-shard step as clusters (lss_shard_cluster_kernel): P CTAs per row, parts of about
-// 32 KB (64 KB at most, 16 CTAs at most), about 4K group maxima per row.  Returns false (and
+// Vocabulary-shard step as clusters (lss_shard_cluster_kernel): P CTAs per row, parts of up to
+// 64 KB (16 CTAs at most; the per-part phases cost more than the bytes, so fewer, larger parts
+// win), about 4K group maxima per row.  Returns false (and
 // launches nothing) when the shard row does not fit or no such cluster can be resident.
 template <int DT>
 static bool launch_shard_cluster(const void* logits, int64_t stride, int B, int Vs, int64_t voff, const float* T,
                                  int K, unsigned char* rec, cudaStream_t st, cudaError_t& err) {
   constexpr int es = DT == LSS_DTYPE_F32 ? 4 : 2;
-  const int P = (int)std::min<int64_t>(SC_MAXCL, std::max<int64_t>(1, ((int64_t)Vs * es + 32767) / 32768));
+  const int P = (int)std::min<int64_t>(SC_MAXCL, std::max<int64_t>(1, ((int64_t)Vs * es + 65535) / 65536));
   const int PS = round_up((Vs + P - 1) / P, 8);
   if ((size_t)PS * es > (size_t)SC_PART_MAX) return false;
   int L = 32;

@@ -732,6 +732,7 @@ __global__ void __launch_bounds__(NT, 2) lss_slow_kernel(const RowArgs a) {
   uint32_t phase = 0;
   for (int i = cid; i < ndefer; i += NC) {
     R.row = a.defer_rows[i];
+    if (R.row < 0) continue;  // a row the latency path finished (the same for the whole cluster)
     slow_row<CL, DT>(R, a, R.row, phase);
     __syncthreads();
   }

@@ -113,6 +113,41 @@ def test_history_on_top_tokens(dtype, V, pad):
 
 
 @needs_cuda
+@pytest.mark.parametrize("name,rows", [
+    ("cfg1", [0]), ("cfg1", [2, 3]), ("cfg1", [1, 4, 5, 6]),            # greedy; top-k 50 + top-p
+    ("cfg2", [0]), ("cfg2", [1, 2, 3, 4]), ("cfg2", [5, 6]),           # bf16, mixed parameters, history
+    ("cfg3", [0]), ("cfg3", [1, 2, 10, 51]),                           # -inf rows, exact max ties
+    ("hist_on_top", [0, 1, 2, 3]),                                     # history on the largest logits
+    ("headline", [7])])
+def test_latency_path_small_batches(name, rows):
+    """Batches of up to four rows take the single-kernel latency path (one cluster per row;
+    rows it cannot bound go to the deferred-row kernel).  Parity on every row, and the greedy
+    and gathered rows stay in that kernel."""
+    w = {"cfg1": lambda: wl.config1(seed=2), "cfg2": lambda: wl.config2(seed=6),
+         "cfg3": lambda: wl.config3(seed=8, B=64), "hist_on_top": lambda: wl.history_on_top(seed=4),
+         "headline": lambda: wl.headline(seed=3, B=16)}[name]().rows(rows)
+    out = G.run(w)
+    assert out["flags"] == 0
+    stats = check_workload(w, out)
+    assert sum(stats.values()) == w.B
+
+
+@needs_cuda
+@pytest.mark.parametrize("V,pad,dtype", [(4099, 3, "f32"), (40_001, 1, "bf16"), (777, 0, "f32"), (151_936, 0, "f16")])
+def test_latency_path_layouts(V, pad, dtype):
+    """The latency path on small and ragged vocabularies, rows that start off a 16-byte
+    boundary, and 16-bit logits."""
+    w = wl.config3(seed=12, B=3, V=V, H=96)
+    w.logits = wl.round_to_dtype(w.logits, dtype)
+    w.top_k[1] = 40
+    w.min_p[2] = 0.0
+    w.temperature[0] = 0.0
+    out = G.run(w, dtype=dtype, row_stride=(V + pad) if pad else None)
+    assert out["flags"] == 0
+    check_workload(w, out)
+
+
+@needs_cuda
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 def test_half_dtypes_match_upcast(dtype):
     w = wl.config1(seed=5)
