@@ -186,7 +186,19 @@ __global__ void __launch_bounds__(NT, 1) lss_row_kernel(const RowArgs a, int TS)
   float tmax = -INFINITY;
   bool nan = false;
   uint64_t best = 0;
-  for (int i = tid; i < n; i += NT) {
+  const int n4 = n >> 2;  // 16-byte groups of the tile, then the last values one by one
+  const float4* t4 = reinterpret_cast<const float4*>(tile);
+  for (int q = tid; q < n4; q += NT) {
+    const float4 v = t4[q];
+    tmax = fmaxf(tmax, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+    nan |= (v.x != v.x) | (v.y != v.y) | (v.z != v.z) | (v.w != v.w);
+    if (greedy) {
+      const int i = lo + 4 * q;
+      best = max(best, max(max(argmax_code(v.x, i), argmax_code(v.y, i + 1)),
+                           max(argmax_code(v.z, i + 2), argmax_code(v.w, i + 3))));
+    }
+  }
+  for (int i = 4 * n4 + tid; i < n; i += NT) {
     const float z = tile[i];
     tmax = fmaxf(tmax, z);
     nan |= z != z;
@@ -213,7 +225,9 @@ __global__ void __launch_bounds__(NT, 1) lss_row_kernel(const RowArgs a, int TS)
   rm = block_allreduce(rm, MaxU64(), r64);
   const uint32_t zk = (uint32_t)rm, sp = (uint32_t)(rm >> 32);
   const int GK = CL * RW_G1;
-  for (int t = tid; t < GK; t += NT) c.allk[t] = cl.map_shared_rank(&c, t / RW_G1)->gk[t % RW_G1];
+  // The group maxima of the row (only top-k rows use them).
+  if (tk_on && !greedy)
+    for (int t = tid; t < GK; t += NT) c.allk[t] = cl.map_shared_rank(&c, t / RW_G1)->gk[t % RW_G1];
   RwCtl* c0 = cl.map_shared_rank(&c, 0);
   // Rank 0's record of the row: the token and path (when `path` is not 0), the deferred-list
   // entry, the flags.
@@ -266,14 +280,18 @@ __global__ void __launch_bounds__(NT, 1) lss_row_kernel(const RowArgs a, int TS)
   }
   // ---- 4. candidates y >= cut0 to rank 0 (z below zlow cannot reach it)
   const float zlow = z_floor_for(key2f(cut0), T);
+  auto is_cand = [&](float z) -> bool {
+    if (!(z >= zlow) || z == -INFINITY) return false;
+    const float y = __fdiv_rn(z, T);
+    return y > -INFINITY && f2key(y) >= cut0;
+  };
   uint32_t cnt = 0;
-  for (int i = tid; i < n; i += NT) {
-    const float z = tile[i];
-    if (z >= zlow && z > -INFINITY) {
-      const float y = __fdiv_rn(z, T);
-      if (y > -INFINITY && f2key(y) >= cut0) ++cnt;
-    }
+  for (int q = tid; q < n4; q += NT) {
+    const float4 v = t4[q];
+    if (fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)) >= zlow)
+      cnt += (is_cand(v.x) ? 1u : 0u) + (is_cand(v.y) ? 1u : 0u) + (is_cand(v.z) ? 1u : 0u) + (is_cand(v.w) ? 1u : 0u);
   }
+  for (int i = 4 * n4 + tid; i < n; i += NT) cnt += is_cand(tile[i]) ? 1u : 0u;
   uint32_t incl = cnt;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -283,17 +301,24 @@ __global__ void __launch_bounds__(NT, 1) lss_row_kernel(const RowArgs a, int TS)
   uint32_t base = 0;
   if (lane == 31 && incl) base = atomicAdd(&c0->n, incl);
   base = __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
-  for (int i = tid; i < n && cnt; i += NT) {
-    const float z = tile[i];
-    if (z >= zlow && z > -INFINITY) {
-      const float y = __fdiv_rn(z, T);
-      const uint32_t yk = f2key(y);
-      if (y > -INFINITY && yk >= cut0) {
-        if (base < (uint32_t)FAST_CAP) c0->G[base] = ((uint64_t)yk << 32) | (uint32_t)(~(uint32_t)(lo + i));
-        ++base;
-        --cnt;
+  auto send = [&](float z, int i) {
+    if (is_cand(z)) {
+      if (base < (uint32_t)FAST_CAP)
+        c0->G[base] = ((uint64_t)f2key(__fdiv_rn(z, T)) << 32) | (uint32_t)(~(uint32_t)(lo + i));
+      ++base;
+    }
+  };
+  if (cnt) {
+    for (int q = tid; q < n4; q += NT) {
+      const float4 v = t4[q];
+      if (fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)) >= zlow) {
+        send(v.x, 4 * q);
+        send(v.y, 4 * q + 1);
+        send(v.z, 4 * q + 2);
+        send(v.w, 4 * q + 3);
       }
     }
+    for (int i = 4 * n4 + tid; i < n; i += NT) send(tile[i], i);
   }
   cl.sync();  // rank 0 holds every candidate
   if (me != 0) {
