@@ -44,7 +44,10 @@ namespace lss {
 constexpr int ST_NW = 16;                     // warps per CTA
 constexpr int ST_NT = ST_NW * 32;
 constexpr int ST_CB = 4096;                   // bytes per chunk
-constexpr int ST_R = 3;                       // ring stages per warp
+// Ring stages per warp.  Two stream faster than three on B200 (the headline pass 32.5 vs 35.6
+// us, 16-bit rows with top-k unchanged) and one is slower (36.2 us): with 32 rather than 48 4 KB
+// copies outstanding per SM the HBM stream runs closer to the copy peak.
+constexpr int ST_R = 2;
 constexpr int ST_NSLOT = 8;                   // slice slots per CTA
 constexpr int ST_SEGCAP = 1024;               // candidate slots per slice
 constexpr int ST_ROWTAB = 64;                 // rows whose parameters a CTA keeps in shared memory
