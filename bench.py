@@ -64,6 +64,18 @@ def algorithmic_bytes(w) -> int:
     return int(w.B * w.V * esize + w.hist_ids.size * 4 + (w.B + 1) * 4 + w.B * (7 * 4 + 4 + 4))
 
 
+def measured_traffic(key: str, scale: float = 1.0):
+    """DRAM bytes (read + write) per launch of a kernel, from one ncu capture recorded in
+    profiles/traffic.json, scaled by this launch's units (rows or shard columns) over the
+    captured launch's; None when no capture is recorded."""
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        rec = json.load(open(tp)).get(key)
+    except (OSError, ValueError):
+        return None
+    return None if rec is None else int(round(rec["bytes_per_launch"] * scale))
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -432,12 +444,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     achieved = alg / (kern_avg_ms / 1000.0) / 1e9
     peak, peak_kind = peaks()
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if args.workload == "headline" and os.path.exists(tp):
-        try:
-            traffic = json.load(open(tp)).get("lss_stream_kernel_headline_bytes_per_launch")
-        except (OSError, ValueError):
-            traffic = None
+    if args.workload == "headline":
+        traffic = measured_traffic("lss_stream_kernel_headline", w.B / B_PER_GPU)
+    elif args.workload == "cfg4":
+        traffic = measured_traffic("lss_stream_kernel_cfg4", w.B / 1024)
 
     # end to end through the public API with host buffers (pinned), copies inside the timing
     e2e = None
@@ -613,7 +623,8 @@ def run_vocab(args, rank: int, world: int, local_rank: int):
             "data": "synthetic (seeded; cfg5)",
             "config": vocab_config(args, w, world), "records_bytes_per_rank": B * rb,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "kernel": "lss_shard_cluster_kernel",
+                         "frac": achieved / peak, "traffic": measured_traffic("lss_shard_cluster_kernel_cfg5", Vs / Vt),
+                         "kernel": "lss_shard_cluster_kernel",
                          "peak_source": peak_kind, "algorithmic_bytes_per_launch": alg, "kernel_ms": kern_ms},
             "clocks": clk, "e2e": None, "cpu_baseline": cpu, "gpu_launches": 2 * args.steps,
         }
