@@ -137,6 +137,51 @@ __device__ __forceinline__ RowPrm make_row_prm(const StreamArgs& a, int row, int
 template <class T, class Op>
 __device__ __forceinline__ T wred(T v, Op op) { return warp_allreduce(v, op); }
 
+// Two 16-bit logits of a word (the lower address in the low half), compared and reduced as a
+// pair: one instruction does the work of two widened f32 operations.
+template <int DT>
+__device__ __forceinline__ uint32_t pk_max(uint32_t a, uint32_t b) {  // NaN-propagating
+  uint32_t r;
+  if constexpr (DT == LSS_DTYPE_BF16) {
+    const __nv_bfloat162 m = __hmax2_nan(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                                         *reinterpret_cast<const __nv_bfloat162*>(&b));
+    r = *reinterpret_cast<const uint32_t*>(&m);
+  } else {
+    const __half2 m = __hmax2_nan(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    r = *reinterpret_cast<const uint32_t*>(&m);
+  }
+  return r;
+}
+template <int DT>
+__device__ __forceinline__ uint32_t pk_ge(uint32_t a, uint32_t lev2) {  // 0xffff per half >= lev
+  if constexpr (DT == LSS_DTYPE_BF16)
+    return __hge2_mask(*reinterpret_cast<const __nv_bfloat162*>(&a), *reinterpret_cast<const __nv_bfloat162*>(&lev2));
+  else
+    return __hge2_mask(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&lev2));
+}
+// The level, in both halves, at or above which a 16-bit value x satisfies the f32 test
+// `x >= lev && x > -inf`: the smallest 16-bit value >= max(lev, -FLT_MAX) (rounding toward
+// +inf is exact here, since x itself is a 16-bit value).  A NaN level matches nothing.
+template <int DT>
+__device__ __forceinline__ uint32_t pk_level(float lev) {
+  uint32_t h;
+  if constexpr (DT == LSS_DTYPE_BF16)
+    h = lev != lev ? 0x7fc0u : (uint32_t)__bfloat16_as_ushort(__float2bfloat16_ru(fmaxf(lev, -FLT_MAX)));
+  else
+    h = lev != lev ? 0x7e00u : (uint32_t)__half_as_ushort(__float2half_ru(fmaxf(lev, -FLT_MAX)));
+  return h | (h << 16);
+}
+template <int DT>
+__device__ __forceinline__ float pk_lo(uint32_t w) {
+  if constexpr (DT == LSS_DTYPE_BF16) return __uint_as_float(w << 16);
+  else return __half2float(__ushort_as_half((uint16_t)(w & 0xffffu)));
+}
+template <int DT>
+__device__ __forceinline__ float pk_hi(uint32_t w) {
+  if constexpr (DT == LSS_DTYPE_BF16) return __uint_as_float(w & 0xffff0000u);
+  else return __half2float(__ushort_as_half((uint16_t)(w >> 16)));
+}
+
 template <int DT>
 __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a) {
   constexpr int ES = DT == LSS_DTYPE_F32 ? 4 : 2;
@@ -355,13 +400,18 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
         float vmx[NV];
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
-          float x[VPV];
-          widen(rv[j], x);
+          if constexpr (DT == LSS_DTYPE_F32) {
+            float x[VPV];
+            widen(rv[j], x);
 #pragma unroll
-          for (int w2 = VPV / 2; w2 >= 1; w2 /= 2)
+            for (int w2 = VPV / 2; w2 >= 1; w2 /= 2)
 #pragma unroll
-            for (int q = 0; q < w2; ++q) x[q] = fmax_nan(x[q], x[q + w2]);
-          vmx[j] = x[0];
+              for (int q = 0; q < w2; ++q) x[q] = fmax_nan(x[q], x[q + w2]);
+            vmx[j] = x[0];
+          } else {  // pairs first, f32 only for the last two values
+            const uint32_t m2 = pk_max<DT>(pk_max<DT>(rv[j].x, rv[j].y), pk_max<DT>(rv[j].z, rv[j].w));
+            vmx[j] = fmax_nan(pk_lo<DT>(m2), pk_hi<DT>(m2));
+          }
         }
         float lm = vmx[0];
 #pragma unroll
@@ -394,12 +444,21 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
             float lowc = fmaxf(zmp, tk0 ? key2f(tk0) : -INFINITY);
             auto count_ge = [&](float lev) -> uint32_t {
               uint32_t cnt = 0;
+              if constexpr (DT == LSS_DTYPE_F32) {
 #pragma unroll
-              for (int j = 0; j < NV; ++j) {
-                float x[VPV];
-                widen(rv[j], x);
+                for (int j = 0; j < NV; ++j) {
+                  float x[VPV];
+                  widen(rv[j], x);
 #pragma unroll
-                for (int q = 0; q < VPV; ++q) cnt += (x[q] >= lev && x[q] > -INFINITY) ? 1u : 0u;
+                  for (int q = 0; q < VPV; ++q) cnt += (x[q] >= lev && x[q] > -INFINITY) ? 1u : 0u;
+                }
+              } else {
+                const uint32_t l2 = pk_level<DT>(lev);
+#pragma unroll
+                for (int j = 0; j < NV; ++j)
+                  cnt += __popc(pk_ge<DT>(rv[j].x, l2)) + __popc(pk_ge<DT>(rv[j].y, l2)) +
+                         __popc(pk_ge<DT>(rv[j].z, l2)) + __popc(pk_ge<DT>(rv[j].w, l2));
+                cnt >>= 4;  // 16 mask bits per value
               }
               return wred(cnt, SumU32());
             };
@@ -429,19 +488,36 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
             const float R0 = key2f(r0);
             const float sb = P.sb;
             uint32_t ab = 0;
+            auto bin = [&](float z) {
+              if (z > R0) {
+                ab++;
+              } else {
+                const float dd = __fmul_rn(__fsub_rn(R0, z), sb);
+                if (dd < (float)NBIN) atomicAdd(&sl->hist[(int)dd], 1u);
+              }
+            };
+            if constexpr (DT == LSS_DTYPE_F32) {
 #pragma unroll
-            for (int j = 0; j < NV; ++j) {
-              float x[VPV];
-              widen(rv[j], x);
+              for (int j = 0; j < NV; ++j) {
+                float x[VPV];
+                widen(rv[j], x);
 #pragma unroll
-              for (int q = 0; q < VPV; ++q) {
-                const float z = x[q];
-                if (!(z >= lowc) || z == -INFINITY) continue;
-                if (z > R0) {
-                  ab++;
-                } else {
-                  const float dd = __fmul_rn(__fsub_rn(R0, z), sb);
-                  if (dd < (float)NBIN) atomicAdd(&sl->hist[(int)dd], 1u);
+                for (int q = 0; q < VPV; ++q) {
+                  const float z = x[q];
+                  if (!(z >= lowc) || z == -INFINITY) continue;
+                  bin(z);
+                }
+              }
+            } else {  // a pair test first; most pairs have no value at or above lowc
+              const uint32_t l2 = pk_level<DT>(lowc);
+#pragma unroll
+              for (int j = 0; j < NV; ++j) {
+                const uint32_t w4[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const uint32_t m = pk_ge<DT>(w4[q], l2);
+                  if (m & 0xffffu) bin(pk_lo<DT>(w4[q]));
+                  if (m >> 16) bin(pk_hi<DT>(w4[q]));
                 }
               }
             }
