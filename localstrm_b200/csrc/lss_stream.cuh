@@ -465,7 +465,8 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
             // A chunk with many values above the slice's threshold (the slice's first chunks)
             // first bounds it with its own values: at least k of them reach `lev`, so the
             // slice's k-th largest does too.
-            if (count_ge(lowc) > 2u * (uint32_t)k && cmax > -INFINITY) {
+            const uint32_t nlow = count_ge(lowc);
+            if (nlow > 2u * (uint32_t)k && cmax > -INFINITY) {
 #pragma unroll 1
               for (float D = 1.0f; D <= 8.0f; D *= 2.0f) {
                 float lev = __fsub_rn(cmax, __fmul_rn(D, T));
@@ -476,94 +477,99 @@ __global__ void __launch_bounds__(ST_NT, 1) lss_stream_kernel(const StreamArgs a
                 }
               }
             }
-            // The histogram's reference: the first running max any warp reports for the slice.
-            uint32_t r0 = *reinterpret_cast<volatile uint32_t*>(&sl->r0key);
-            if (r0 == 0u) {
-              if (lane == 0) {
-                const uint32_t old = atomicCAS(&sl->r0key, 0u, mk);
-                r0 = old ? old : mk;
-              }
-              r0 = __shfl_sync(0xffffffffu, r0, 0);
-            }
-            const float R0 = key2f(r0);
-            const float sb = P.sb;
-            uint32_t ab = 0;
-            auto bin = [&](float z) {
-              if (z > R0) {
-                ab++;
-              } else {
-                const float dd = __fmul_rn(__fsub_rn(R0, z), sb);
-                if (dd < (float)NBIN) atomicAdd(&sl->hist[(int)dd], 1u);
-              }
-            };
-            if constexpr (DT == LSS_DTYPE_F32) {
-#pragma unroll
-              for (int j = 0; j < NV; ++j) {
-                float x[VPV];
-                widen(rv[j], x);
-#pragma unroll
-                for (int q = 0; q < VPV; ++q) {
-                  const float z = x[q];
-                  if (!(z >= lowc) || z == -INFINITY) continue;
-                  bin(z);
-                }
-              }
-            } else {  // a pair test first; most pairs have no value at or above lowc
-              const uint32_t l2 = pk_level<DT>(lowc);
-#pragma unroll
-              for (int j = 0; j < NV; ++j) {
-                const uint32_t w4[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  const uint32_t m = pk_ge<DT>(w4[q], l2);
-                  if (m & 0xffffu) bin(pk_lo<DT>(w4[q]));
-                  if (m >> 16) bin(pk_hi<DT>(w4[q]));
-                }
-              }
-            }
-            ab = wred(ab, SumU32());
-            if (lane == 0 && ab) atomicAdd(&sl->above, ab);
-            __syncwarp();
-            // Bins as counted so far by every warp (lane l reads bins 8l .. 8l+7).  A partial
-            // view only counts fewer values, so the threshold stays a lower bound.
-            const volatile uint32_t* vh = sl->hist;
-            uint32_t c8[8];
-            uint32_t loc = 0;
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              c8[q] = vh[8 * lane + q];
-              loc += c8[q];
-            }
-            uint32_t incl = loc;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-              const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-              if (lane >= o) incl += y;
-            }
-            const uint32_t abv = *reinterpret_cast<volatile uint32_t*>(&sl->above);
+            // A chunk without a value at or above lowc adds nothing to the histogram: it keeps
+            // tau = lowc (the slice's threshold as last published, or the min-p floor) and leaves
+            // refreshing the threshold from the bins to the warps that add counts.
             float tau = lowc;
-            if (abv >= (uint32_t)k) {
-              tau = fmaxf(tau, R0);
-            } else {
-              const unsigned hit = __ballot_sync(0xffffffffu, abv + incl >= (uint32_t)k);
-              if (hit) {
-                const int L = __ffs(hit) - 1;
-                int b = 0;
-                uint32_t acc = abv + incl - loc;
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                  acc += c8[q];
-                  if (acc < (uint32_t)k) b = q + 1;
+            if (nlow != 0u) {
+              // The histogram's reference: the first running max any warp reports for the slice.
+              uint32_t r0 = *reinterpret_cast<volatile uint32_t*>(&sl->r0key);
+              if (r0 == 0u) {
+                if (lane == 0) {
+                  const uint32_t old = atomicCAS(&sl->r0key, 0u, mk);
+                  r0 = old ? old : mk;
                 }
-                const int bk = __shfl_sync(0xffffffffu, 8 * lane + b, L);
-                // The k-th largest counted value lies in bin bk: (R0 - z) * sb < bk + 1.  One
-                // more bin of slack covers the rounding of the bins.
-                float zw = __fsub_rn(R0, __fmul_rn((float)(bk + 2), P.binw));
-                zw = __fsub_rn(zw, fabsf(zw) * 2.384185791015625e-07f + 1e-37f);
-                tau = fmaxf(tau, zw);
+                r0 = __shfl_sync(0xffffffffu, r0, 0);
               }
+              const float R0 = key2f(r0);
+              const float sb = P.sb;
+              uint32_t ab = 0;
+              auto bin = [&](float z) {
+                if (z > R0) {
+                  ab++;
+                } else {
+                  const float dd = __fmul_rn(__fsub_rn(R0, z), sb);
+                  if (dd < (float)NBIN) atomicAdd(&sl->hist[(int)dd], 1u);
+                }
+              };
+              if constexpr (DT == LSS_DTYPE_F32) {
+  #pragma unroll
+                for (int j = 0; j < NV; ++j) {
+                  float x[VPV];
+                  widen(rv[j], x);
+  #pragma unroll
+                  for (int q = 0; q < VPV; ++q) {
+                    const float z = x[q];
+                    if (!(z >= lowc) || z == -INFINITY) continue;
+                    bin(z);
+                  }
+                }
+              } else {  // a pair test first; most pairs have no value at or above lowc
+                const uint32_t l2 = pk_level<DT>(lowc);
+  #pragma unroll
+                for (int j = 0; j < NV; ++j) {
+                  const uint32_t w4[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
+  #pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    const uint32_t m = pk_ge<DT>(w4[q], l2);
+                    if (m & 0xffffu) bin(pk_lo<DT>(w4[q]));
+                    if (m >> 16) bin(pk_hi<DT>(w4[q]));
+                  }
+                }
+              }
+              ab = wred(ab, SumU32());
+              if (lane == 0 && ab) atomicAdd(&sl->above, ab);
+              __syncwarp();
+              // Bins as counted so far by every warp (lane l reads bins 8l .. 8l+7).  A partial
+              // view only counts fewer values, so the threshold stays a lower bound.
+              const volatile uint32_t* vh = sl->hist;
+              uint32_t c8[8];
+              uint32_t loc = 0;
+  #pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                c8[q] = vh[8 * lane + q];
+                loc += c8[q];
+              }
+              uint32_t incl = loc;
+  #pragma unroll
+              for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+              }
+              const uint32_t abv = *reinterpret_cast<volatile uint32_t*>(&sl->above);
+              if (abv >= (uint32_t)k) {
+                tau = fmaxf(tau, R0);
+              } else {
+                const unsigned hit = __ballot_sync(0xffffffffu, abv + incl >= (uint32_t)k);
+                if (hit) {
+                  const int L = __ffs(hit) - 1;
+                  int b = 0;
+                  uint32_t acc = abv + incl - loc;
+  #pragma unroll
+                  for (int q = 0; q < 8; ++q) {
+                    acc += c8[q];
+                    if (acc < (uint32_t)k) b = q + 1;
+                  }
+                  const int bk = __shfl_sync(0xffffffffu, 8 * lane + b, L);
+                  // The k-th largest counted value lies in bin bk: (R0 - z) * sb < bk + 1.  One
+                  // more bin of slack covers the rounding of the bins.
+                  float zw = __fsub_rn(R0, __fmul_rn((float)(bk + 2), P.binw));
+                  zw = __fsub_rn(zw, fabsf(zw) * 2.384185791015625e-07f + 1e-37f);
+                  tau = fmaxf(tau, zw);
+                }
+              }
+              if (lane == 0 && tau > -INFINITY) atomicMax(&sl->taukey, f2key(tau));
             }
-            if (lane == 0 && tau > -INFINITY) atomicMax(&sl->taukey, f2key(tau));
             thr = fmaxf(thr, tau);
           }
           // ---- candidates: finite z >= thr, into the slice's segment.  Each lane marks its
