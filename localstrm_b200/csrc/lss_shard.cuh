@@ -36,7 +36,6 @@ __global__ void __launch_bounds__(NT) lss_shard_kernel(const void* logits, int64
   constexpr int ES = DT == LSS_DTYPE_F32 ? 4 : 2;
   __shared__ uint64_t C[SHARD_CAND];
   __shared__ uint32_t HLw[NWARP][NBIN + 1];
-  __shared__ uint32_t r32[NWARP];
   __shared__ float rf[NWARP];
   __shared__ double rd[NWARP];
   __shared__ uint64_t r64[NWARP];
